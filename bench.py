@@ -1,0 +1,381 @@
+#!/usr/bin/env python
+"""Benchmark: DeepSeek-V3 routed MoE layer forward on B200.
+
+Workload ("cfg1"): T=4096 tokens per GPU, hidden 7168,
+256 routed experts, moe_intermediate 2048, bf16 weights ~ N(0, 0.02), top-8
+sigmoid routing with 8 groups / 4 kept, renormalised x2.5.  One step =
+gating -> permute -> gate/up GEMM + SwiGLU -> down GEMM -> weighted unpermute
+on one batch of synthetic tokens (seeded randn, no dataset).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`value` is whole-job tokens/s with inputs resident in HBM, timed with CUDA
+events over exactly K steps between barriers, max over ranks.  `e2e` is the
+same metric through the public MoELayer call with pinned host buffers: each
+step copies hidden + logits host->device and the layer output device->host.
+The 22.5 GB of expert weights streamed every step exceed the 126 MB L2, so no
+flush is needed.  `--impl reference` times the CPU restatement of the
+reference's torch path (the oracle port) on the host cores.  With N > 1 each
+rank runs its own layer replica (weak scaling, no data-path collective).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+T_TOKENS, HIDDEN, INTER, EXPERTS, TOPK, N_GROUP, TOPK_GROUP, RSF = 4096, 7168, 2048, 256, 8, 8, 4, 2.5
+METRIC = "MoE-layer tokens/s"
+UNIT = "tokens/s"
+WORKLOAD = ("cfg1: DeepSeek-V3 routed MoE layer forward (gating, permute, gate/up GEMM + "
+            "SwiGLU, down GEMM, weighted unpermute), T=4096 tokens/GPU, H=7168, I=2048, "
+            "E=256, top-8, 8 groups / 4 kept, bf16 weights")
+LAUNCHES_PER_STEP = 6  # gating, route, row copy, gate/up GEMM, down GEMM, unpermute
+STAGES = ("gating", "route", "row_copy", "gate_up_swiglu_gemm", "down_gemm", "unpermute")
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        for r in self.rows:
+            for name, v in zip(self.REASONS, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle port of the reference's torch path
+# ---------------------------------------------------------------------------
+
+def cpu_layer_sample(logits, bias, hidden_bf16_f32, n_experts_sample, seed=0):
+    """Times the CPU restatement of the layer on a bounded sample: gating,
+    permute and unpermute over all tokens, the expert FFN on the rows of
+    `n_experts_sample` experts; returns (estimated seconds for the full
+    layer, description)."""
+    from oracle import moe_oracle as O
+    t0 = time.perf_counter()
+    w, idx = O.topk_gating(logits, bias, TOPK, N_GROUP, TOPK_GROUP, RSF, True)
+    t1 = time.perf_counter()
+    permuted, offsets, s2d, _ = O.moe_permute(hidden_bf16_f32, idx, EXPERTS)
+    t2 = time.perf_counter()
+    rng = np.random.default_rng(seed)
+    counts = np.diff(offsets)
+    experts = rng.choice(np.nonzero(counts)[0], size=n_experts_sample, replace=False)
+    y = np.zeros(permuted.shape, dtype=np.uint16)
+    ffn = 0.0
+    rows = 0
+    for j, e in enumerate(experts):
+        g = np.random.default_rng(1000 + int(e))
+        w_gu = O.bf16_round((g.standard_normal((2 * INTER, HIDDEN), dtype=np.float32) * 0.02))
+        w_dn = O.bf16_round((g.standard_normal((HIDDEN, INTER), dtype=np.float32) * 0.02))
+        s, t = int(offsets[e]), int(offsets[e + 1])
+        if j == 0:  # first BLAS call of the process: thread-pool start-up, untimed
+            O.expert_ffn(permuted[s:s + 1], w_gu, w_dn, gemm_dtype=np.float32)
+        f0 = time.perf_counter()
+        y[s:t] = O.bf16_bits(O.expert_ffn(permuted[s:t], w_gu, w_dn, gemm_dtype=np.float32))
+        ffn += time.perf_counter() - f0
+        rows += t - s
+    t3 = time.perf_counter()
+    O.moe_unpermute(y, w, s2d, idx.shape[0], TOPK)
+    t4 = time.perf_counter()
+    total_rows = int(offsets[-1])
+    est = (t1 - t0) + (t2 - t1) + ffn * total_rows / max(rows, 1) + (t4 - t3)
+    desc = (f"oracle port on the host: gating, permute and unpermute over all {idx.shape[0]} "
+            f"tokens; expert FFN (fp32 GEMMs, as ref_grouped_gemm) timed on {rows} rows of {n_experts_sample} experts "
+            f"and scaled to all {total_rows} rows")
+    return est, desc
+
+
+def cpu_inputs():
+    from layerstormexpertkernels_b200.synthetic import token_inputs
+    x = token_inputs(T_TOKENS, EXPERTS, HIDDEN, seed=0)
+    return x.logits.numpy(), x.bias.numpy(), x.hidden.float().numpy()
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import torch
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    logits, bias, hidden = cpu_inputs()
+    per_step = []
+    desc = ""
+    for i in range(args.warmup + args.steps):
+        est, desc = cpu_layer_sample(logits, bias, hidden, n_experts_sample=2, seed=i)
+        if i >= args.warmup:
+            per_step.append(est)
+    sec = statistics.mean(per_step)
+    value = T_TOKENS / sec
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens": T_TOKENS, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def load_traffic():
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import layerstormexpertkernels_b200 as P
+    from layerstormexpertkernels_b200.synthetic import expert_weights, token_inputs
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    T = args.tokens
+    w_gu, w_down = expert_weights(EXPERTS, HIDDEN, INTER, device=dev)
+    x = token_inputs(T, EXPERTS, HIDDEN, seed=rank)
+    layer = P.MoELayer(w_gu, w_down, x.bias.to(dev), topk=TOPK, n_group=N_GROUP,
+                       topk_group=TOPK_GROUP, routed_scaling_factor=RSF, renormalize=True,
+                       max_tokens=T)
+    hidden, logits = x.hidden.to(dev), x.logits.to(dev)
+    out = torch.empty_like(hidden)
+    tw = torch.empty(T, TOPK, dtype=torch.float32, device=dev)
+    ti = torch.empty(T, TOPK, dtype=torch.int32, device=dev)
+
+    for _ in range(args.warmup):
+        layer(hidden, logits, out=out, topk_weights=tw, topk_indices=ti)
+    torch.cuda.synchronize()
+    if P.device_error() != 0:
+        raise RuntimeError("a kernel reported a device-side error during warm-up")
+    rows_per_expert = torch.bincount(ti.flatten().long(), minlength=EXPERTS).cpu().numpy()
+
+    # ---- timed region: K steps, stage events recorded on the launch stream
+    stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)]
+                for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    start.record()
+    for i in range(args.steps):
+        layer(hidden, logits, out=out, stage_events=stage_ev[i])
+    end.record()
+    torch.cuda.synchronize()
+    sampler.stop()
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    stage_ms = {s: statistics.mean(stage_ev[i][j].elapsed_time(stage_ev[i][j + 1])
+                                   for i in range(args.steps)) for j, s in enumerate(STAGES)}
+    if P.device_error() != 0:
+        raise RuntimeError("a kernel reported a device-side error in the timed region")
+
+    # ---- end to end through the public call, host buffers, copies timed
+    hidden_h = x.hidden.pin_memory()
+    logits_h = x.logits.pin_memory()
+    out_h = torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    for _ in range(2):
+        hidden.copy_(hidden_h, non_blocking=True)
+        logits.copy_(logits_h, non_blocking=True)
+        layer(hidden, logits, out=out)
+        out_h.copy_(out, non_blocking=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        hidden.copy_(hidden_h, non_blocking=True)
+        logits.copy_(logits_h, non_blocking=True)
+        layer(hidden, logits, out=out)
+        out_h.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    peaks = load_peaks()
+    rows = T * TOPK
+    touched = int((rows_per_expert > 0).sum())
+    # Algorithmic bytes of the dominant kernel (gate/up GEMM + SwiGLU): the
+    # weights of every touched expert once, the permuted rows once, the
+    # activations written once.
+    gu_bytes = touched * 2 * INTER * HIDDEN * 2 + rows * HIDDEN * 2 + rows * INTER * 2
+    gu_flops = 2.0 * rows * HIDDEN * 2 * INTER
+    dn_bytes = touched * HIDDEN * INTER * 2 + rows * INTER * 2 + rows * HIDDEN * 2
+    dn_flops = 2.0 * rows * INTER * HIDDEN
+    stage_bytes = {
+        "gating": T * EXPERTS * 4 + EXPERTS * 4 + T * TOPK * 8,
+        "route": T * TOPK * 4 * 3 + (EXPERTS + 1) * 4,
+        "row_copy": T * HIDDEN * 2 + rows * HIDDEN * 2,
+        "gate_up_swiglu_gemm": gu_bytes,
+        "down_gemm": dn_bytes,
+        "unpermute": rows * HIDDEN * 2 + T * TOPK * 8 + T * HIDDEN * 2,
+    }
+    stages = {s: {"ms": stage_ms[s], "gbs": stage_bytes[s] / (stage_ms[s] * 1e-3) / 1e9,
+                  "bytes": stage_bytes[s]} for s in STAGES}
+    stages["gate_up_swiglu_gemm"]["tflops"] = gu_flops / (stage_ms["gate_up_swiglu_gemm"] * 1e-3) / 1e12
+    stages["down_gemm"]["tflops"] = dn_flops / (stage_ms["down_gemm"] * 1e-3) / 1e12
+    dom = "gate_up_swiglu_gemm"
+    achieved = stages[dom]["gbs"]
+    traffic = load_traffic().get(dom, {}).get("bytes_per_launch")
+    roofline = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                "peak_source": peaks["source"], "traffic": traffic,
+                "algorithmic_bytes": gu_bytes,
+                "tensor_tflops": stages[dom]["tflops"],
+                "tensor_frac_of_sustained": stages[dom]["tflops"] / peaks["bf16_tflops_sustained"]}
+
+    line = {"metric": METRIC, "value": world * T / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded randn tokens; per-expert seeded N(0,0.02) bf16 weights)",
+            "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "global_tokens": world * T,
+                       "hidden": HIDDEN, "inter": INTER, "experts": EXPERTS, "topk": TOPK,
+                       "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "inputs larger than L2: 22.5 GB of expert weights per step"},
+            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+            "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": T * HIDDEN * 2 + T * EXPERTS * 4,
+                    "d2h_bytes_per_step": T * HIDDEN * 2},
+            "roofline": roofline,
+            "stages": stages,
+            "clocks": sampler.summary()}
+    if world == 1 and not args.no_cpu_baseline:
+        import torch as _t
+        cores = len(os.sched_getaffinity(0))
+        _t.set_num_threads(cores)
+        logits_np, bias_np, hidden_np = cpu_inputs()
+        est, desc = cpu_layer_sample(logits_np, bias_np, hidden_np, n_experts_sample=4)
+        line["cpu_baseline"] = {"value": T_TOKENS / est, "unit": UNIT, "cores": cores,
+                                "kind": "port", "sample": desc}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=T_TOKENS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("note: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,245 @@
+/*
+ * lsek.h — C ABI of the B200 (sm_100a) MoE expert-kernel library (liblsek.so).
+ *
+ * Every entry point takes plain device pointers, sizes and a `void* stream`
+ * (a cudaStream_t), launches asynchronously on that stream and returns an
+ * lsek_status.  Nothing here allocates device memory: outputs and scratch
+ * ("workspace") buffers are owned by the caller, with a size-query function
+ * for each entry point that needs scratch.  The library keeps no per-call
+ * state, so entry points are safe to call from several host threads on
+ * different streams.
+ *
+ * Each entry point replaces one launcher of the reference library
+ * (kkontosis/LayerStoRmExpertKernels, namespace layerstorm::compute); the
+ * replaced interface is cited as file:line beside each declaration.  Shapes
+ * and argument meanings are the reference's.  Three differences, all
+ * deliberate:
+ *   - errors come back as status codes (the reference throws C++ exceptions
+ *     and never checks launch errors);
+ *   - limits the reference leaves unchecked (topk <= 8 in unpermute, topk
+ *     within the kept groups, experts per lane) are validated;
+ *   - fp16 is computed as fp16 (the reference runs its bf16 kernel on fp16
+ *     data).
+ */
+#ifndef LSEK_H_
+#define LSEK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LSEK_ABI_VERSION 1
+
+/* Entry points are the only symbols liblsek.so exports. */
+#if defined(__GNUC__)
+#define LSEK_API __attribute__((visibility("default")))
+#else
+#define LSEK_API
+#endif
+
+/* Status codes.  INVALID_ARG maps to Python ValueError in the torch binding,
+ * the rest to RuntimeError. */
+typedef enum lsek_status {
+  LSEK_OK = 0,
+  LSEK_ERR_INVALID_ARG = 1, /* bad shape / parameter (reference: std::invalid_argument) */
+  LSEK_ERR_UNSUPPORTED = 2, /* valid request this build does not implement (dtype, size) */
+  LSEK_ERR_CUDA = 3,        /* a CUDA runtime call or kernel launch failed */
+  LSEK_ERR_DEVICE = 4       /* a kernel reported a device-side error (bounded wait expired) */
+} lsek_status;
+
+/* Element types of activation tensors. */
+typedef enum lsek_dtype {
+  LSEK_BF16 = 0,
+  LSEK_FP16 = 1,
+  LSEK_FP32 = 2
+} lsek_dtype;
+
+/* Scoring functions (reference: sm120/gating/topk_gating.h:19 ScoringFunc). */
+typedef enum lsek_scoring_func {
+  LSEK_SCORING_SIGMOID = 0,
+  LSEK_SCORING_SQRTSOFTPLUS = 1
+} lsek_scoring_func;
+
+/* Top-k gating parameters (reference: sm120/gating/topk_gating.h:22-31
+ * TopkGatingParams). */
+typedef struct lsek_topk_gating_params {
+  int32_t num_tokens;
+  int32_t num_experts;
+  int32_t topk;                 /* experts selected per token */
+  int32_t n_group;              /* expert groups; 1 = flat top-k */
+  int32_t topk_group;           /* groups kept before the expert top-k (n_group > 1) */
+  float routed_scaling_factor;  /* weights scaled so they sum to this (renormalize) */
+  int32_t renormalize;          /* nonzero: w *= routed_scaling_factor / sum(w) */
+  int32_t scoring_func;         /* lsek_scoring_func */
+} lsek_topk_gating_params;
+
+/* ---- library info ------------------------------------------------------ */
+
+/* Message describing the last non-OK status returned on the calling thread. */
+LSEK_API const char* lsek_last_error(void);
+/* Version string, e.g. "lsek 0.1.0 sm_100a". */
+LSEK_API const char* lsek_version(void);
+/* Reads and clears the device-side error word that kernels set when a
+ * bounded wait expires (synchronises `stream`).  *code receives 0 when no
+ * kernel reported an error since the last call. */
+LSEK_API lsek_status lsek_device_error(int32_t* code, void* stream);
+
+/* ---- gating -------------------------------------------------------------- */
+
+/* Top-k gating (grouped when n_group > 1).  logits [T,E] f32 row-major,
+ * bias [E] f32 or NULL (selection only), outputs [T,topk] f32 / int32 in
+ * selection order (descending biased score, ties to the lower expert id).
+ * Limits: E <= 1024, topk <= 32, n_group <= 32, E % n_group == 0,
+ * topk <= topk_group * (E / n_group).
+ * Replaces launch_topk_gating (sm120/gating/topk_gating.h:43-46,
+ * sm120/gating/topk_gating.cu:391-443). */
+LSEK_API lsek_status lsek_topk_gating(float* topk_weights, int32_t* topk_indices,
+                             const float* logits, const float* bias,
+                             const lsek_topk_gating_params* params,
+                             void* stream);
+
+/* Adaptive gating: per token, sort (weight, index) by weight descending
+ * (stable), keep the shortest prefix whose cumulative weight reaches
+ * threshold * total, pad the rest with (0.0, -1).  topk in [1, 32],
+ * threshold in [0, 1].  Replaces launch_adaptive_gating
+ * (smxx/gating/adaptive_gating.h:34-39, adaptive_gating.cu:94-118). */
+LSEK_API lsek_status lsek_adaptive_gating(float* out_weights, int32_t* out_indices,
+                                 int32_t* expert_counts,
+                                 const float* in_weights,
+                                 const int32_t* in_indices, int32_t num_tokens,
+                                 int32_t topk, double threshold, void* stream);
+
+/* ---- permute / unpermute -------------------------------------------------- */
+
+/* Scratch bytes lsek_moe_permute needs for these sizes.  Replaces
+ * query_moe_permute_workspace_size (smxx/permute/moe_permute.h:25-26). */
+LSEK_API size_t lsek_moe_permute_workspace_size(int32_t max_tokens, int32_t max_topk,
+                                       int32_t num_experts);
+
+/* Stable counting-sort permute.  topk_indices [T,topk] int32; an index
+ * outside [0,E) (the adaptive-gating sentinel -1) is treated as expert E and
+ * sorts last.  Outputs: permuted [T*topk, H] (rows grouped by expert, within
+ * an expert in ascending t*topk+slot order), expert_offsets [E+1]
+ * (offsets[E] = number of valid slots), src_to_dest_map [T*topk],
+ * permuted_idx [T*topk].  elem_size_bytes is 2 or 4 (bitwise row copy).
+ * E <= 1023.  Replaces launch_moe_permute (smxx/permute/moe_permute.h:42-55,
+ * moe_permute.cu:518-600). */
+LSEK_API lsek_status lsek_moe_permute(void* permuted_input, int32_t* expert_offsets,
+                             int32_t* src_to_dest_map, int32_t* permuted_idx,
+                             const void* hidden_states,
+                             const int32_t* topk_indices, int32_t num_tokens,
+                             int32_t topk, int32_t hidden_dim,
+                             int32_t num_experts, int32_t elem_size_bytes,
+                             void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/* Weighted unpermute.  fp32_output == 0: out [T,H] (dtype) =
+ * round(sum_k fma(w[t,k], x[s2d[t,k]], acc)), fp32 accumulation in slot order.
+ * fp32_output != 0: out is f32 [T,topk,H], out[t,k,:] = w[t,k]*x[s2d[t,k]]
+ * (no cross-slot sum).  topk <= 32.  Replaces launch_moe_unpermute
+ * (smxx/permute/moe_permute.h:79-89, moe_permute.cu:602-642). */
+LSEK_API lsek_status lsek_moe_unpermute(void* output, const void* permuted_output,
+                               const float* topk_weights,
+                               const int32_t* src_to_dest_map,
+                               int32_t num_tokens, int32_t topk,
+                               int32_t hidden_dim, int32_t dtype,
+                               int32_t fp32_output, void* stream);
+
+/* Per-slot unpermute with a 16-bit payload: out [T,topk,H] (dtype),
+ * out[t,k,:] = round(w[t,k] * x[s2d[t,k]]).  Replaces
+ * launch_moe_unpermute_bf16_perslot (smxx/permute/moe_permute.h:100-109,
+ * moe_permute.cu:644-672). */
+LSEK_API lsek_status lsek_moe_unpermute_perslot(void* output,
+                                       const void* permuted_output,
+                                       const float* topk_weights,
+                                       const int32_t* src_to_dest_map,
+                                       int32_t num_tokens, int32_t topk,
+                                       int32_t hidden_dim, int32_t dtype,
+                                       void* stream);
+
+/* Fixed-order slot reduce: out[t,h] = round_bf16(sum_{k=0..topk-1} in[t,k,h])
+ * with the sum taken in fp32 from 0.0f in slot order.  in_dtype is
+ * LSEK_FP32 or LSEK_BF16; out is bf16.  Replaces
+ * launch_moe_combine_reduce_slots_fp32_to_bf16 and
+ * launch_moe_combine_reduce_slots_bf16_to_bf16
+ * (smxx/permute/moe_permute.h:116-134, moe_permute.cu:674-710). */
+LSEK_API lsek_status lsek_moe_combine_reduce_slots(void* output_bf16,
+                                          const void* input_perslot,
+                                          int32_t num_tokens, int32_t topk,
+                                          int32_t hidden_dim, int32_t in_dtype,
+                                          void* stream);
+
+/* ---- activation ----------------------------------------------------------- */
+
+/* Fused SwiGLU: out [N,d] = silu(g) * u with g = in[:, :d], u = in[:, d:],
+ * computed in fp32, stored in dtype.  swiglu_limit > 0 clamps
+ * g = min(g, L), u = clamp(u, -L, L) first.  Replaces launch_fused_swiglu
+ * (smxx/activation/fused_swiglu.h:22-27, fused_swiglu.cu:156-183). */
+LSEK_API lsek_status lsek_fused_swiglu(void* output, const void* input,
+                              int32_t num_tokens, int32_t d,
+                              float swiglu_limit, int32_t dtype, void* stream);
+
+/* ---- expert contraction (tcgen05 / TMEM / TMA) -------------------------- */
+
+/* Grouped bf16 GEMM over experts: for each expert e,
+ *   D[r, :] = A[r, :] . B[e]^T   for r in [offsets[e], offsets[e+1])
+ * A [rows, K] bf16 row-major, B [E, N, K] bf16 (row-major per expert),
+ * D [rows, N] bf16, fp32 accumulation.  Rows outside every expert range are
+ * not written.  K % 8 == 0, N % 32 == 0, A/B/D 16-byte aligned.
+ * The reference documents this contraction (USAGE.md:40-57) and tests it
+ * with ref_grouped_gemm (tests/test_reference.py:228-254) but ships the
+ * kernel in a separate library; argument order follows USAGE.md:122-126. */
+LSEK_API lsek_status lsek_grouped_gemm_bf16(void* D, const void* A, const void* B,
+                                   const int32_t* expert_offsets,
+                                   int32_t num_experts, int32_t rows,
+                                   int32_t N, int32_t K, void* stream);
+
+/* Gate/up grouped GEMM with the SwiGLU in its epilogue.  W_gu [E, 2I, K]
+ * holds gate rows 0..I-1 and up rows I..2I-1 per expert.  For each row r of
+ * expert e: g = bf16(A[r].Wg^T), u = bf16(A[r].Wu^T) and
+ * Hout[r, :] = swiglu(g, u, swiglu_limit) as in lsek_fused_swiglu, so the
+ * result equals lsek_grouped_gemm_bf16 followed by lsek_fused_swiglu.
+ * Hout [rows, I] bf16.  I % 32 == 0. */
+LSEK_API lsek_status lsek_grouped_gemm_swiglu_bf16(void* Hout, const void* A,
+                                          const void* W_gu,
+                                          const int32_t* expert_offsets,
+                                          int32_t num_experts, int32_t rows,
+                                          int32_t I, int32_t K,
+                                          float swiglu_limit, void* stream);
+
+/* ---- whole MoE layer ------------------------------------------------------ */
+
+/* Scratch bytes for lsek_moe_layer_forward. */
+LSEK_API size_t lsek_moe_layer_workspace_size(int32_t num_tokens, int32_t hidden_dim,
+                                     int32_t inter_dim, int32_t num_experts,
+                                     int32_t topk);
+
+/* Number of stages of lsek_moe_layer_forward, for stage_events. */
+#define LSEK_LAYER_STAGES 6
+
+/* DeepSeek-V3-style routed-expert layer, all on `stream`:
+ *   topk_gating -> route -> row copy -> gate/up GEMM + SwiGLU ->
+ *   down GEMM -> weighted unpermute.
+ * hidden [T,H] bf16, logits [T,E] f32, bias [E] f32 or NULL,
+ * W_gu [E, 2I, H] bf16, W_down [E, H, I] bf16, out [T,H] bf16.
+ * topk_weights/topk_indices ([T,topk]) may be NULL; when given they receive
+ * the routing.  stage_events is NULL or an array of LSEK_LAYER_STAGES + 1
+ * cudaEvent_t that are recorded on `stream` before each stage and after the
+ * last, for per-stage timing.  The composition follows the reference's
+ * documented flow (USAGE.md:40-57) with the oracle ref_expert_forward
+ * (tests/test_reference.py:257-276) generalised to top-k. */
+LSEK_API lsek_status lsek_moe_layer_forward(
+    void* out, const void* hidden, const float* logits, const float* bias,
+    const void* W_gu, const void* W_down, const lsek_topk_gating_params* gp,
+    int32_t hidden_dim, int32_t inter_dim, float swiglu_limit,
+    float* topk_weights, int32_t* topk_indices, void* workspace,
+    size_t workspace_bytes, void* const* stage_events, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* LSEK_H_ */

@@ -1,0 +1,327 @@
+// Top-k gating and adaptive gating for sm_100a.
+//
+// Top-k gating keeps one token per warp.  Lane l owns the EPL consecutive
+// experts [l*EPL, (l+1)*EPL), loaded with 16-byte vector loads, so one warp
+// reads a token's logits row as one contiguous 1 KB (E=256) burst and every
+// later phase runs in registers:
+//   1. score   s = sigmoid(x) or sqrt(softplus(x)); sel = s + bias
+//   2. groups  (n_group > 1) per-group sum of the top-2 sel values, then each
+//              lane g computes its group's rank among all groups with
+//              shuffles (ties go to the lower group) and a ballot gives the
+//              kept-group mask; experts of dropped groups leave the race
+//   3. top-k   topk rounds of a warp arg-max on (order-preserving key of sel,
+//              expert id), ties to the lower id; the owning lane retires its
+//              winner and rescans its EPL candidates
+//   4. weights unbiased score of each winner, summed in selection order,
+//              optional w *= routed_scaling_factor / sum
+// This follows ref_topk_gating (tests/test_reference.py:133-187) and the
+// selection order of warp_topk_select (sm120/gating/topk_gating.cu:105-139).
+// The reference kernel instead runs one 256-thread block per token with four
+// block barriers and a serial thread-0 group pick (topk_gating.cu:244-388).
+//
+// Scores use exp evaluated in double precision and rounded once to fp32, then
+// fp32 add and fp32 division: s = 1 / (1 + e^-x).  That is the exact formula
+// of torch.sigmoid rounded at each fp32 step; it removes any dependence on a
+// particular single-precision exp implementation.
+#include <float.h>
+
+#include "common.cuh"
+
+namespace lsek {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ float score_sigmoid(float x) {
+  const float e = static_cast<float>(exp(-static_cast<double>(x)));
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+}
+
+// sqrt(softplus(x)) with torch's softplus threshold: x > 20 -> x, else
+// log1p(exp(x)); each step rounded to fp32 as torch does.
+__device__ __forceinline__ float score_sqrtsoftplus(float x) {
+  if (x > 20.0f) return __fsqrt_rn(x);
+  const float e = static_cast<float>(exp(static_cast<double>(x)));
+  const float l = static_cast<float>(log1p(static_cast<double>(e)));
+  return __fsqrt_rn(l);
+}
+
+// Maps fp32 to uint32 so that unsigned order equals float order
+// (-inf < ... < -0 < +0 < ... < +inf).  Key 0 is reserved for "not a
+// candidate" (no float maps below 0x007fffff).
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(256) topk_gating_kernel(
+    float* __restrict__ out_w, int32_t* __restrict__ out_i,
+    const float* __restrict__ logits, const float* __restrict__ bias, int T,
+    int E, int topk, int n_group, int topk_group, float rsf, int renorm,
+    int scoring, int vec_ok) {
+  extern __shared__ float s_group[];  // per warp: sel values, padded 33/32
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int warps_per_block = blockDim.x >> 5;
+  const int pad_stride = E + (E >> 5) + 1;
+  float* s_sel = s_group + warp * pad_stride;
+  const int e0 = lane * EPL;
+  const int epg = E / n_group;
+
+  // Bias is the same for every token: keep this lane's slice in registers.
+  float b[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = e0 + j;
+    b[j] = (bias != nullptr && e < E) ? bias[e] : 0.0f;
+  }
+
+  for (int t = blockIdx.x * warps_per_block + warp; t < T;
+       t += gridDim.x * warps_per_block) {
+    const float* row = logits + static_cast<int64_t>(t) * E;
+    float x[EPL];
+    if (EPL >= 4 && vec_ok && e0 + EPL <= E) {
+#pragma unroll
+      for (int j = 0; j < EPL; j += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(row + e0 + j));
+        x[j] = v.x; x[j + 1] = v.y; x[j + 2] = v.z; x[j + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) x[j] = (e0 + j < E) ? __ldg(row + e0 + j) : 0.0f;
+    }
+
+    float sc[EPL];
+    uint32_t key[EPL];
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) {
+      const int e = e0 + j;
+      const float s = scoring == LSEK_SCORING_SIGMOID ? score_sigmoid(x[j])
+                                                      : score_sqrtsoftplus(x[j]);
+      const float sel = (bias != nullptr) ? __fadd_rn(s, b[j]) : s;
+      sc[j] = s;
+      key[j] = (e < E) ? order_key(sel) : 0u;
+      if (n_group > 1 && e < E) s_sel[e + (e >> 5)] = sel;
+    }
+
+    if (n_group > 1) {
+      __syncwarp();
+      float gscore = 0.0f;
+      if (lane < n_group) {
+        float top1 = -INFINITY, top2 = -INFINITY;
+        const int gb = lane * epg;
+        for (int i = 0; i < epg; ++i) {
+          const int e = gb + i;
+          const float v = s_sel[e + (e >> 5)];
+          if (v > top1) {
+            top2 = top1;
+            top1 = v;
+          } else if (v > top2) {
+            top2 = v;
+          }
+        }
+        gscore = (epg >= 2) ? __fadd_rn(top1, top2) : top1;
+      }
+      int rank = 0;
+      for (int h = 0; h < n_group; ++h) {
+        const float o = __shfl_sync(kFull, gscore, h);
+        rank += (o > gscore) || (o == gscore && h < lane);
+      }
+      const unsigned kept = __ballot_sync(kFull, lane < n_group && rank < topk_group);
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) {
+        const int e = e0 + j;
+        if (e < E && !((kept >> (e / epg)) & 1u)) key[j] = 0u;
+      }
+      __syncwarp();  // s_sel is rewritten by the next token
+    }
+
+    // Local best: highest key, lowest j on ties (lowest expert id).
+    uint32_t bk = 0;
+    int bj = -1;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j)
+      if (key[j] > bk) { bk = key[j]; bj = j; }
+
+    float wsum = 0.0f;
+    float my_w = 0.0f;
+    int my_i = 0;
+    for (int k = 0; k < topk; ++k) {
+      uint32_t kk = bk;
+      int ie = (bj >= 0) ? e0 + bj : 0x7fffffff;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const uint32_t ok = __shfl_xor_sync(kFull, kk, off);
+        const int oi = __shfl_xor_sync(kFull, ie, off);
+        if (ok > kk || (ok == kk && oi < ie)) { kk = ok; ie = oi; }
+      }
+      const int owner = ie / EPL;
+      float mine = 0.0f;
+#pragma unroll
+      for (int j = 0; j < EPL; ++j)
+        if (j == bj) mine = sc[j];
+      const float wv = __shfl_sync(kFull, mine, owner);
+      if (lane == owner) {
+#pragma unroll
+        for (int j = 0; j < EPL; ++j)
+          if (j == bj) key[j] = 0u;
+        bk = 0;
+        bj = -1;
+#pragma unroll
+        for (int j = 0; j < EPL; ++j)
+          if (key[j] > bk) { bk = key[j]; bj = j; }
+      }
+      wsum = __fadd_rn(wsum, wv);
+      if (lane == k) { my_w = wv; my_i = ie; }
+    }
+    if (renorm && wsum > 0.0f) my_w = __fmul_rn(my_w, __fdiv_rn(rsf, wsum));
+    if (lane < topk) {
+      out_w[static_cast<int64_t>(t) * topk + lane] = my_w;
+      out_i[static_cast<int64_t>(t) * topk + lane] = my_i;
+    }
+  }
+}
+
+template <int EPL>
+cudaError_t launch_topk(float* w, int32_t* idx, const float* logits,
+                        const float* bias, const lsek_topk_gating_params& p,
+                        int vec_ok, cudaStream_t st) {
+  const int threads = 256;
+  const int warps = threads / 32;
+  const size_t smem =
+      p.n_group > 1 ? static_cast<size_t>(warps) * (p.num_experts + (p.num_experts >> 5) + 1) * sizeof(float)
+                    : 0;
+  const int blocks_needed = static_cast<int>(ceil_div(p.num_tokens, warps));
+  const int grid = blocks_needed < num_sms() * 8 ? blocks_needed : num_sms() * 8;
+  topk_gating_kernel<EPL><<<grid, threads, smem, st>>>(
+      w, idx, logits, bias, p.num_tokens, p.num_experts, p.topk,
+      p.n_group > 1 ? p.n_group : 1, p.topk_group, p.routed_scaling_factor,
+      p.renormalize, p.scoring_func, vec_ok);
+  return cudaGetLastError();
+}
+
+// One thread per token.  Stable insertion sort by weight (descending), then
+// the cumulative threshold scan of ref_adaptive_gating
+// (tests/test_reference.py:190-225): the total is an fp32 sum, target and
+// running sum are formed in double as the reference's Python loop does.
+template <int KMAX>
+__global__ void adaptive_gating_kernel(float* __restrict__ ow,
+                                       int32_t* __restrict__ oi,
+                                       int32_t* __restrict__ counts,
+                                       const float* __restrict__ iw,
+                                       const int32_t* __restrict__ ii, int T,
+                                       int topk, double threshold) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  float w[KMAX];
+  int32_t id[KMAX];
+  const int64_t base = static_cast<int64_t>(t) * topk;
+  for (int k = 0; k < topk; ++k) {
+    const float wk = iw[base + k];
+    const int32_t ik = ii[base + k];
+    int j = k - 1;
+    while (j >= 0 && w[j] < wk) {
+      w[j + 1] = w[j];
+      id[j + 1] = id[j];
+      --j;
+    }
+    w[j + 1] = wk;
+    id[j + 1] = ik;
+  }
+  float total = 0.0f;
+  for (int k = 0; k < topk; ++k) total = __fadd_rn(total, w[k]);
+  const double target = threshold * static_cast<double>(total);
+  double cum = 0.0;
+  int count = topk;
+  for (int k = 0; k < topk; ++k) {
+    cum += static_cast<double>(w[k]);
+    if (cum >= target) {
+      count = k + 1;
+      break;
+    }
+  }
+  if (count < 1) count = 1;
+  for (int k = 0; k < topk; ++k) {
+    ow[base + k] = k < count ? w[k] : 0.0f;
+    oi[base + k] = k < count ? id[k] : -1;
+  }
+  counts[t] = count;
+}
+
+}  // namespace
+}  // namespace lsek
+
+extern "C" lsek_status lsek_topk_gating(float* topk_weights,
+                                        int32_t* topk_indices,
+                                        const float* logits, const float* bias,
+                                        const lsek_topk_gating_params* params,
+                                        void* stream) {
+  using namespace lsek;
+  LSEK_REQUIRE(params != nullptr, "topk_gating: params is NULL");
+  const lsek_topk_gating_params& p = *params;
+  LSEK_REQUIRE(p.num_tokens >= 0, "topk_gating: num_tokens must be >= 0");
+  if (p.num_tokens == 0) return LSEK_OK;
+  LSEK_REQUIRE(p.num_experts > 0, "topk_gating: num_experts must be > 0");
+  LSEK_REQUIRE(p.topk >= 1 && p.topk <= p.num_experts,
+               "topk_gating: topk must be in [1, num_experts]");
+  LSEK_REQUIRE(p.n_group >= 1 && p.num_experts % p.n_group == 0,
+               "topk_gating: num_experts must be divisible by n_group");
+  if (p.n_group > 1) {
+    LSEK_REQUIRE(p.topk_group >= 1 && p.topk_group <= p.n_group,
+                 "topk_gating: topk_group must be in [1, n_group]");
+    LSEK_REQUIRE(p.topk <= p.topk_group * (p.num_experts / p.n_group),
+                 "topk_gating: topk (%d) exceeds the experts of the kept groups (%d)",
+                 p.topk, p.topk_group * (p.num_experts / p.n_group));
+    LSEK_REQUIRE(p.n_group <= 32, "topk_gating: n_group must be <= 32");
+  }
+  LSEK_REQUIRE(p.scoring_func == LSEK_SCORING_SIGMOID ||
+                   p.scoring_func == LSEK_SCORING_SQRTSOFTPLUS,
+               "topk_gating: scoring_func must be sigmoid (0) or sqrtsoftplus (1)");
+  if (p.num_experts > 1024 || p.topk > 32)
+    return fail(LSEK_ERR_UNSUPPORTED, "topk_gating: supports num_experts <= 1024 and topk <= 32");
+  LSEK_REQUIRE(topk_weights && topk_indices && logits, "topk_gating: NULL tensor pointer");
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int vec_ok = (p.num_experts % 4 == 0) &&
+                     (reinterpret_cast<uintptr_t>(logits) % 16 == 0);
+  const int epl = static_cast<int>(ceil_div(p.num_experts, 32));
+  cudaError_t e;
+  if (epl <= 1)       e = launch_topk<1>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+  else if (epl <= 2)  e = launch_topk<2>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+  else if (epl <= 4)  e = launch_topk<4>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+  else if (epl <= 8)  e = launch_topk<8>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+  else if (epl <= 16) e = launch_topk<16>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+  else                e = launch_topk<32>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+  if (e != cudaSuccess) return fail(LSEK_ERR_CUDA, "topk_gating: %s", cudaGetErrorString(e));
+  return LSEK_OK;
+}
+
+extern "C" lsek_status lsek_adaptive_gating(float* out_weights,
+                                            int32_t* out_indices,
+                                            int32_t* expert_counts,
+                                            const float* in_weights,
+                                            const int32_t* in_indices,
+                                            int32_t num_tokens, int32_t topk,
+                                            double threshold, void* stream) {
+  using namespace lsek;
+  LSEK_REQUIRE(num_tokens >= 0, "adaptive_gating: num_tokens must be >= 0");
+  if (num_tokens == 0) return LSEK_OK;
+  LSEK_REQUIRE(topk >= 1 && topk <= 32, "adaptive_gating: topk must be in [1, 32]");
+  LSEK_REQUIRE(threshold >= 0.0 && threshold <= 1.0,
+               "adaptive_gating: threshold must be in [0.0, 1.0]");
+  LSEK_REQUIRE(out_weights && out_indices && expert_counts && in_weights && in_indices,
+               "adaptive_gating: NULL tensor pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int threads = 128;
+  const int grid = static_cast<int>(ceil_div(num_tokens, threads));
+  if (topk <= 8)
+    adaptive_gating_kernel<8><<<grid, threads, 0, st>>>(out_weights, out_indices, expert_counts,
+                                                         in_weights, in_indices, num_tokens, topk,
+                                                         threshold);
+  else
+    adaptive_gating_kernel<32><<<grid, threads, 0, st>>>(out_weights, out_indices, expert_counts,
+                                                          in_weights, in_indices, num_tokens, topk,
+                                                          threshold);
+  return check_launch("adaptive_gating");
+}

@@ -1,0 +1,621 @@
+// Grouped bf16 expert GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// Problem: for every expert e, D[rows of e] = A[rows of e] . B[e]^T, where
+// A [rows, K] holds the permuted token rows (expert-contiguous, ranges from
+// expert_offsets) and B [E, Nb, K] the expert weights, both K-major bf16.
+// This is the contraction of ref_grouped_gemm (tests/test_reference.py:228-254)
+// and of the expert FFN flow in USAGE.md:40-57.
+//
+// Tiling.  A tile is 128 rows x 256 B-rows x all of K.  Work units are
+// (expert, n-tile, m-tile) in that nesting, m fastest, so the m-tiles that
+// share one weight tile are taken by neighbouring CTAs at the same time and
+// the weight tile is read from HBM once (the second read hits L2); the 16-28
+// n-tiles of one expert reuse its A rows from L2.  A persistent grid of one
+// CTA per SM walks the unit list with a static stride.  At DeepSeek-V3 shape
+// the kernel is bound by streaming the 22.5 GB of weights from HBM.
+//
+// One CTA = 6 warps:
+//   warp 0      TMA producer: per k-block loads A [128 x 64] and two B boxes
+//               [128 x 64] into a 4-stage ring (128-byte swizzle), completing
+//               on the stage's `full` mbarrier.
+//   warp 1      MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=16) per stage into
+//               one of two TMEM accumulators (2 x 256 fp32 columns = all 512
+//               columns); tcgen05.commit frees the stage and, after the last
+//               k-block, signals the accumulator full.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM
+//               lanes 32*(w%4)..+31 = its 32 rows), convert, store to global,
+//               then release the accumulator; it overlaps the next tile's
+//               main loop thanks to the second accumulator.
+// SWIGLU mode stacks 128 gate rows (rows n*128 of the expert) and the matching
+// 128 up rows (rows I + n*128) as the two B boxes, so one N=256 MMA yields g
+// and u for 128 output columns; the epilogue rounds both to bf16 and applies
+// swiglu_f32, which makes the result bit-identical to the plain GEMM followed
+// by the standalone fused_swiglu kernel.
+//
+// Every mbarrier wait is bounded (kWaitLimitNs).  A role whose wait expires
+// records a device error, raises the CTA abort flag and leaves its loop; the
+// producer then waits (bounded) for the loads it issued, the MMA warp for its
+// outstanding MMAs, and warp 1 frees TMEM before the CTA exits.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "swiglu.cuh"
+
+namespace lsek {
+
+// Device-side error word (see DeviceError in common.cuh).
+__device__ int32_t g_device_error = 0;
+
+__device__ __forceinline__ void report_device_error(int32_t code) {
+  atomicCAS(&g_device_error, 0, code);
+}
+
+namespace gemm {
+
+constexpr int kBM = 128;                       // UMMA M, rows per tile
+constexpr int kBK = 64;                        // K per stage = one 128-byte swizzle row
+constexpr int kBN = 256;                       // UMMA N
+constexpr int kBoxRows = 128;                  // rows per TMA box
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK * 2;         // 16 KB
+constexpr int kBoxBytes = kBoxRows * kBK * 2;  // 16 KB
+constexpr int kStageBytes = kABytes + 2 * kBoxBytes;  // 48 KB
+constexpr int kTmemCols = 2 * kBN;             // two accumulators
+constexpr int kThreads = 192;
+constexpr int kMaxExperts = 1024;
+
+// M=128, N=256, A/B bf16 K-major, D fp32 (tcgen05 instruction descriptor:
+// D format bits 4-5, A format bits 7-9, B format bits 10-12, N>>3 bits 17-22,
+// M>>4 bits 24-28).
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
+                            (static_cast<uint32_t>(kBN >> 3) << 17) |
+                            (static_cast<uint32_t>(kBM >> 4) << 24);
+
+struct Params {
+  const int32_t* offsets;  // [E+1]
+  int num_experts;
+  int rows;                // rows of A and D
+  int num_kb;              // ceil(K / kBK)
+  int n_tiles;             // n-tiles per expert
+  int b_rows;              // B rows per expert
+  int b_tile_rows;         // first-box row step per n-tile
+  int b_second;            // row offset of the second box
+  __nv_bfloat16* D;
+  int64_t ldd;
+  int out_tile_cols;       // output columns per tile
+  int n_out;               // output width
+  float swiglu_limit;
+};
+
+struct Smem {
+  uint8_t tiles[kStages][kStageBytes];  // 1024-byte aligned (base is aligned)
+  uint64_t full_bar[kStages];
+  uint64_t empty_bar[kStages];
+  uint64_t acc_full_bar[2];
+  uint64_t acc_empty_bar[2];
+  uint64_t mma_done_bar;
+  uint32_t tmem_base;
+  int32_t abort;
+  int32_t warp_tot[kThreads / 32];
+  int32_t offs[kMaxExperts + 1];
+  int32_t cum[kMaxExperts + 1];
+};
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+
+// ---- PTX wrappers ----------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for phase `parity` of `bar`.  Gives up when another role has aborted
+// (honor_abort) or after kWaitLimitNs, recording `code`.
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int32_t* abort,
+                                       int32_t code, bool honor_abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (honor_abort && *abort) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      report_device_error(code);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Shared-memory matrix descriptor: K-major tile of 128-byte rows with the
+// 128-byte swizzle; 8-row groups 1024 bytes apart (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32"
+      " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+__device__ __forceinline__ float round_bf16(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ int mtiles_of(const Smem& s, int e) {
+  const int n = s.offs[e + 1] - s.offs[e];
+  return n > 0 ? (n + kBM - 1) / kBM : 0;
+}
+
+// Maps a unit id to (expert, m-tile, n-tile): the largest e with cum[e] <= id
+// is the (non-empty) expert that owns it.
+__device__ __forceinline__ void decode_unit(const Smem& s, int num_experts, int id, int& e,
+                                            int& m, int& n) {
+  int lo = 0, hi = num_experts - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s.cum[mid] <= id) lo = mid;
+    else hi = mid - 1;
+  }
+  e = lo;
+  const int local = id - s.cum[e];
+  const int mt = mtiles_of(s, e);
+  n = local / mt;
+  m = local - n * mt;
+}
+
+template <bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                        const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                     ~static_cast<uintptr_t>(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int E = p.num_experts;
+
+  // ---- unit table: cum[e] = sum over e' < e of m-tiles(e') * n_tiles -------
+  // Offsets are clamped to [0, rows]; an expert whose end precedes its start
+  // has no tiles, so every stored row stays inside D.
+  for (int i = tid; i <= E; i += kThreads) {
+    int v = __ldg(p.offsets + i);
+    v = v < 0 ? 0 : (v > p.rows ? p.rows : v);
+    s.offs[i] = v;
+  }
+  if (tid == 0) s.abort = 0;
+  __syncthreads();
+  {
+    const int per = (E + kThreads - 1) / kThreads;
+    const int eb = tid * per;
+    const int ee = min(E, eb + per);
+    int local = 0;
+    for (int e = eb; e < ee; ++e) local += mtiles_of(s, e) * p.n_tiles;
+    int incl = local;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    if (lane == 31) s.warp_tot[warp] = incl;
+    __syncthreads();
+    int run = incl - local;
+    for (int w = 0; w < warp; ++w) run += s.warp_tot[w];
+    for (int e = eb; e < ee; ++e) {
+      s.cum[e] = run;
+      run += mtiles_of(s, e) * p.n_tiles;
+    }
+    if (eb < E && ee == E) s.cum[E] = run;
+  }
+
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full_bar[i], 1);
+      mbar_init(&s.empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full_bar[i], 1);
+      mbar_init(&s.acc_empty_bar[i], 4);
+    }
+    mbar_init(&s.mma_done_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem_base = s.tmem_base;
+  const int total = s.cum[E];
+  volatile int32_t* abort = &s.abort;
+
+  if (warp == 0) {
+    // ===================== TMA producer =====================
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_a = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      uint32_t last_phase[kStages] = {0, 0, 0, 0};
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
+        int e, m, n;
+        decode_unit(s, E, unit, e, m, n);
+        const int row0 = s.offs[e] + m * kBM;
+        const int brow = e * p.b_rows + n * p.b_tile_rows;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&s.empty_bar[stage], phase ^ 1u, abort, kDevErrGemmProducerWait, true)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a = s.tiles[stage];
+          mbar_expect_tx(&s.full_bar[stage], kStageBytes);
+          tma_load_2d(a, &tmap_a, &s.full_bar[stage], kb * kBK, row0, pol_a);
+          tma_load_2d(a + kABytes, &tmap_b, &s.full_bar[stage], kb * kBK, brow, pol_w);
+          tma_load_2d(a + kABytes + kBoxBytes, &tmap_b, &s.full_bar[stage], kb * kBK,
+                      brow + p.b_second, pol_w);
+          issued |= 1u << stage;
+          last_phase[stage] = phase;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {  // let every issued load land before the CTA can exit
+        for (int st = 0; st < kStages; ++st)
+          if (issued & (1u << st))
+            mbar_wait(&s.full_bar[st], last_phase[st], abort, kDevErrGemmProducerWait, false);
+      }
+    }
+  } else if (warp == 1) {
+    // ===================== MMA issuer =====================
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&s.acc_empty_bar[acc], acc_phase ^ 1u, abort, kDevErrGemmMmaWait, true)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&s.full_bar[stage], phase, abort, kDevErrGemmMmaWait, true)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(s.tiles[stage]);
+          const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_bf16(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
+                      kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          umma_commit(&s.empty_bar[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&s.acc_full_bar[acc]);
+      }
+      // Outstanding MMAs read shared memory and write TMEM: finish them first.
+      umma_commit(&s.mma_done_bar);
+      mbar_wait(&s.mma_done_bar, 0, abort, kDevErrGemmMmaWait, false);
+    }
+  } else {
+    // ===================== epilogue (warps 2..5) =====================
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int it = 0;
+    for (int unit = blockIdx.x; unit < total; unit += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&s.acc_full_bar[acc], acc_phase, abort, kDevErrGemmEpilogueWait, true)) break;
+      tc_fence_after();
+      int e, m, n;
+      decode_unit(s, E, unit, e, m, n);
+      const int r = s.offs[e] + m * kBM + q * 32 + lane;
+      const bool valid = r < s.offs[e + 1];
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kBN);
+      const int col0 = n * p.out_tile_cols;
+      const int cols_here = min(p.out_tile_cols, p.n_out - col0);
+      __nv_bfloat16* drow = p.D + static_cast<int64_t>(valid ? r : 0) * p.ldd + col0;
+      if (SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < kBoxRows; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tbase + c, g);
+          tmem_ld32(tbase + kBoxRows + c, u);
+          tmem_ld_wait();
+          if (valid && c < cols_here) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float h0 = swiglu_f32(round_bf16(__uint_as_float(g[2 * j])),
+                                          round_bf16(__uint_as_float(u[2 * j])), p.swiglu_limit);
+              const float h1 = swiglu_f32(round_bf16(__uint_as_float(g[2 * j + 1])),
+                                          round_bf16(__uint_as_float(u[2 * j + 1])),
+                                          p.swiglu_limit);
+              packed[j] = pack_bf16x2(h0, h1);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(drow + c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                                  packed[4 * j + 3]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < kBN; c += 32) {
+          uint32_t v[32];
+          tmem_ld32(tbase + c, v);
+          tmem_ld_wait();
+          if (valid && c < cols_here) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              packed[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+            uint4* dst = reinterpret_cast<uint4*>(drow + c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                                  packed[4 * j + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty_bar[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---- host side -----------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 2-D bf16 map over a [outer, inner] row-major tensor, box [kBoxRows, kBK],
+// 128-byte swizzle, zero fill out of bounds.
+lsek_status make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(LSEK_ERR_CUDA, "grouped_gemm: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(kBoxRows)};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                        strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(LSEK_ERR_CUDA, "grouped_gemm: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return LSEK_OK;
+}
+
+template <bool SWIGLU>
+lsek_status launch(void* D, const void* A, const void* B, const int32_t* offsets, int E, int rows,
+                   int n_out, int b_rows, int K, float limit, cudaStream_t st) {
+  static PerDeviceOnce attrs;
+  const cudaError_t ae = once_per_device(attrs, [] {
+    return cudaFuncSetAttribute(grouped_gemm_kernel<SWIGLU>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kSmemBytes));
+  });
+  if (ae != cudaSuccess) return fail(LSEK_ERR_CUDA, "grouped_gemm: %s", cudaGetErrorString(ae));
+  CUtensorMap ma, mb;
+  lsek_status s = make_map(&ma, A, static_cast<uint64_t>(K), static_cast<uint64_t>(rows));
+  if (s != LSEK_OK) return s;
+  s = make_map(&mb, B, static_cast<uint64_t>(K), static_cast<uint64_t>(E) * b_rows);
+  if (s != LSEK_OK) return s;
+  Params p;
+  p.offsets = offsets;
+  p.num_experts = E;
+  p.rows = rows;
+  p.num_kb = static_cast<int>(ceil_div(K, kBK));
+  p.D = static_cast<__nv_bfloat16*>(D);
+  p.ldd = n_out;
+  p.n_out = n_out;
+  p.b_rows = b_rows;
+  p.swiglu_limit = limit;
+  if (SWIGLU) {
+    p.n_tiles = static_cast<int>(ceil_div(n_out, kBoxRows));
+    p.b_tile_rows = kBoxRows;
+    p.b_second = n_out;  // up rows start at I
+    p.out_tile_cols = kBoxRows;
+  } else {
+    p.n_tiles = static_cast<int>(ceil_div(n_out, kBN));
+    p.b_tile_rows = kBN;
+    p.b_second = kBoxRows;
+    p.out_tile_cols = kBN;
+  }
+  const int64_t max_units = (ceil_div(rows, kBM) + E) * static_cast<int64_t>(p.n_tiles);
+  const int grid = static_cast<int>(max_units < num_sms() ? max_units : num_sms());
+  grouped_gemm_kernel<SWIGLU><<<grid, kThreads, kSmemBytes, st>>>(ma, mb, p);
+  return check_launch(SWIGLU ? "grouped_gemm_swiglu_bf16" : "grouped_gemm_bf16");
+}
+
+lsek_status validate(const char* name, const void* D, const void* A, const void* B,
+                     const int32_t* offsets, int E, int rows, int n_out, int K) {
+  LSEK_REQUIRE(E >= 1, "%s: num_experts must be >= 1", name);
+  LSEK_REQUIRE(rows >= 0 && n_out >= 0 && K >= 0, "%s: sizes must be >= 0", name);
+  if (E > kMaxExperts) return fail(LSEK_ERR_UNSUPPORTED, "%s: num_experts must be <= %d", name, kMaxExperts);
+  LSEK_REQUIRE(K % 8 == 0, "%s: K must be a multiple of 8 (16-byte rows), got %d", name, K);
+  LSEK_REQUIRE(n_out % 32 == 0, "%s: output width must be a multiple of 32, got %d", name, n_out);
+  LSEK_REQUIRE(offsets != nullptr, "%s: expert_offsets is NULL", name);
+  LSEK_REQUIRE(D && A && B, "%s: NULL tensor pointer", name);
+  LSEK_REQUIRE(reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(B) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(D) % 16 == 0,
+               "%s: A, B and D must be 16-byte aligned", name);
+  return LSEK_OK;
+}
+
+}  // namespace gemm
+
+// Used by the layer forward.
+lsek_status grouped_gemm_plain(void* D, const void* A, const void* B, const int32_t* offsets, int E,
+                               int rows, int N, int K, cudaStream_t st) {
+  if (rows == 0 || N == 0) return LSEK_OK;
+  return gemm::launch<false>(D, A, B, offsets, E, rows, N, N, K, 0.0f, st);
+}
+lsek_status grouped_gemm_swiglu(void* H, const void* A, const void* Wgu, const int32_t* offsets,
+                                int E, int rows, int I, int K, float limit, cudaStream_t st) {
+  if (rows == 0 || I == 0) return LSEK_OK;
+  return gemm::launch<true>(H, A, Wgu, offsets, E, rows, I, 2 * I, K, limit, st);
+}
+
+}  // namespace lsek
+
+extern "C" lsek_status lsek_device_error(int32_t* code, void* stream) {
+  using namespace lsek;
+  LSEK_REQUIRE(code != nullptr, "lsek_device_error: code is NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  LSEK_CUDA_TRY(cudaStreamSynchronize(st));
+  int32_t zero = 0;
+  LSEK_CUDA_TRY(cudaMemcpyFromSymbol(code, g_device_error, sizeof(int32_t)));
+  LSEK_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int32_t)));
+  return LSEK_OK;
+}
+
+extern "C" lsek_status lsek_grouped_gemm_bf16(void* D, const void* A, const void* B,
+                                              const int32_t* expert_offsets, int32_t num_experts,
+                                              int32_t rows, int32_t N, int32_t K, void* stream) {
+  using namespace lsek;
+  lsek_status s = gemm::validate("grouped_gemm_bf16", D, A, B, expert_offsets, num_experts, rows, N, K);
+  if (s != LSEK_OK) return s;
+  LSEK_REQUIRE(static_cast<int64_t>(num_experts) * N < (1ll << 31),
+               "grouped_gemm_bf16: num_experts * N must fit in int32");
+  return grouped_gemm_plain(D, A, B, expert_offsets, num_experts, rows, N, K,
+                            static_cast<cudaStream_t>(stream));
+}
+
+extern "C" lsek_status lsek_grouped_gemm_swiglu_bf16(void* Hout, const void* A, const void* W_gu,
+                                                     const int32_t* expert_offsets,
+                                                     int32_t num_experts, int32_t rows, int32_t I,
+                                                     int32_t K, float swiglu_limit, void* stream) {
+  using namespace lsek;
+  lsek_status s =
+      gemm::validate("grouped_gemm_swiglu_bf16", Hout, A, W_gu, expert_offsets, num_experts, rows, I, K);
+  if (s != LSEK_OK) return s;
+  LSEK_REQUIRE(swiglu_limit >= 0.0f, "grouped_gemm_swiglu_bf16: swiglu_limit must be >= 0");
+  LSEK_REQUIRE(static_cast<int64_t>(num_experts) * 2 * I < (1ll << 31),
+               "grouped_gemm_swiglu_bf16: num_experts * 2I must fit in int32");
+  return grouped_gemm_swiglu(Hout, A, W_gu, expert_offsets, num_experts, rows, I, K, swiglu_limit,
+                             static_cast<cudaStream_t>(stream));
+}
