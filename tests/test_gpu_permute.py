@@ -183,9 +183,12 @@ def check_swiglu(out, gate, up, limit):
     ref = O.swiglu(gate.float().numpy(), up.float().numpy(), limit)
     got = out.float().cpu().numpy().astype(np.float64)
     # One rounding to the 16-bit format of a value within a few fp32 ulps of
-    # the exact result: at most one 16-bit ulp away from it.
+    # the exact result: at most one 16-bit ulp away from it.  Below 2^-100
+    # fp32's e^-g overflows for g < -88.7 and silu(g) flushes to 0, as the
+    # reference's torch F.silu does; the double-precision oracle keeps the
+    # tiny value, so those elements only need to be tiny.
     if out.dtype == torch.bfloat16:
-        ulp = np.maximum(np.abs(ref) * 2.0 ** -7, 2.0 ** -133)
+        ulp = np.maximum(np.abs(ref) * 2.0 ** -7, 2.0 ** -100)
     else:
         ulp = np.maximum(np.abs(ref) * 2.0 ** -10, 2.0 ** -24)
     assert (np.abs(got - ref) <= ulp).all(), np.abs(got - ref).max()
