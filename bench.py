@@ -233,8 +233,9 @@ def run_ours(args):
         return float(t.item())
 
     T = args.tokens
-    w_gu, w_down = expert_weights(EXPERTS, HIDDEN, INTER, device=dev)
-    x = token_inputs(T, EXPERTS, HIDDEN, seed=rank)
+    E = args.experts
+    w_gu, w_down = expert_weights(E, HIDDEN, INTER, device=dev)
+    x = token_inputs(T, E, HIDDEN, seed=rank)
     layer = P.MoELayer(w_gu, w_down, x.bias.to(dev), topk=TOPK, n_group=N_GROUP,
                        topk_group=TOPK_GROUP, routed_scaling_factor=RSF, renormalize=True,
                        max_tokens=T)
@@ -248,11 +249,10 @@ def run_ours(args):
     torch.cuda.synchronize()
     if P.device_error() != 0:
         raise RuntimeError("a kernel reported a device-side error during warm-up")
-    rows_per_expert = torch.bincount(ti.flatten().long(), minlength=EXPERTS).cpu().numpy()
+    rows_per_expert = torch.bincount(ti.flatten().long(), minlength=E).cpu().numpy()
 
     # ---- timed region: K steps, stage events recorded on the launch stream
-    stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)]
-                for _ in range(args.steps)]
+    stage_ev = [P.StageEvents() for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local)
     barrier()
@@ -267,8 +267,8 @@ def run_ours(args):
     sampler.stop()
     barrier()
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
-    stage_ms = {s: statistics.mean(stage_ev[i][j].elapsed_time(stage_ev[i][j + 1])
-                                   for i in range(args.steps)) for j, s in enumerate(STAGES)}
+    per_step = [ev.elapsed_ms() for ev in stage_ev]
+    stage_ms = {s: statistics.mean(d[s] for d in per_step) for s in STAGES}
     if P.device_error() != 0:
         raise RuntimeError("a kernel reported a device-side error in the timed region")
 
@@ -311,8 +311,8 @@ def run_ours(args):
     dn_bytes = touched * HIDDEN * INTER * 2 + rows * INTER * 2 + rows * HIDDEN * 2
     dn_flops = 2.0 * rows * INTER * HIDDEN
     stage_bytes = {
-        "gating": T * EXPERTS * 4 + EXPERTS * 4 + T * TOPK * 8,
-        "route": T * TOPK * 4 * 3 + (EXPERTS + 1) * 4,
+        "gating": T * E * 4 + E * 4 + T * TOPK * 8,
+        "route": T * TOPK * 4 * 3 + (E + 1) * 4,
         "row_copy": T * HIDDEN * 2 + rows * HIDDEN * 2,
         "gate_up_swiglu_gemm": gu_bytes,
         "down_gemm": dn_bytes,
@@ -336,18 +336,20 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded randn tokens; per-expert seeded N(0,0.02) bf16 weights)",
-            "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "global_tokens": world * T,
-                       "hidden": HIDDEN, "inter": INTER, "experts": EXPERTS, "topk": TOPK,
+            "config": {"workload": WORKLOAD if (T, E) == (T_TOKENS, EXPERTS) else
+                       f"profiling case: T={T}, E={E} (cfg1 otherwise)",
+                       "tokens_per_gpu": T, "global_tokens": world * T,
+                       "hidden": HIDDEN, "inter": INTER, "experts": E, "topk": TOPK,
                        "parallelism": "replicas" if world > 1 else "single",
                        "l2": "inputs larger than L2: 22.5 GB of expert weights per step"},
             "gpu_launches": LAUNCHES_PER_STEP * args.steps,
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": UNIT,
-                    "h2d_bytes_per_step": T * HIDDEN * 2 + T * EXPERTS * 4,
+                    "h2d_bytes_per_step": T * HIDDEN * 2 + T * E * 4,
                     "d2h_bytes_per_step": T * HIDDEN * 2},
             "roofline": roofline,
             "stages": stages,
             "clocks": sampler.summary()}
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and (T, E) == (T_TOKENS, EXPERTS):
         import torch as _t
         cores = len(os.sched_getaffinity(0))
         _t.set_num_threads(cores)
@@ -367,6 +369,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=T_TOKENS)
+    ap.add_argument("--experts", type=int, default=EXPERTS,
+                    help="routed experts (default 256); smaller values make profiling cases")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

@@ -89,7 +89,8 @@ def build_ext(force: bool = False) -> str:
            + ["-I" + i for i in incs] + ["-L" + d for d in libdirs]
            + ["-L" + PKG, "-llsek", "-Wl,-rpath,$ORIGIN"]
            + ["-Wl,-rpath," + d for d in libdirs]
-           + ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python"])
+           + ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
+              "-lcudart"])
     _run(cmd)
     return EXT
 

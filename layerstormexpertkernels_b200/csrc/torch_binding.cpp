@@ -9,6 +9,7 @@
 // reference's launchers do via pybind11's exception translation.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime_api.h>
 #include <pybind11/stl.h>
 #include <torch/extension.h>
 
@@ -366,6 +367,37 @@ void moe_layer_forward_out(torch::Tensor out, torch::Tensor hidden, torch::Tenso
       stream_of(hidden)));
 }
 
+// Timing events for lsek_moe_layer_forward's stage_events: created with
+// timing enabled, recorded by the library on the layer's stream, read back
+// as milliseconds between consecutive events.
+std::vector<int64_t> events_create(int64_t n) {
+  std::vector<int64_t> out;
+  for (int64_t i = 0; i < n; ++i) {
+    cudaEvent_t e = nullptr;
+    TORCH_CHECK(cudaEventCreate(&e) == cudaSuccess, "events_create: cudaEventCreate failed");
+    out.push_back(reinterpret_cast<int64_t>(e));
+  }
+  return out;
+}
+
+std::vector<double> events_elapsed_ms(std::vector<int64_t> handles) {
+  std::vector<double> out;
+  for (size_t i = 0; i + 1 < handles.size(); ++i) {
+    auto a = reinterpret_cast<cudaEvent_t>(handles[i]);
+    auto b = reinterpret_cast<cudaEvent_t>(handles[i + 1]);
+    TORCH_CHECK(cudaEventSynchronize(b) == cudaSuccess, "events_elapsed_ms: synchronize failed");
+    float ms = 0.0f;
+    TORCH_CHECK(cudaEventElapsedTime(&ms, a, b) == cudaSuccess,
+                "events_elapsed_ms: event not recorded");
+    out.push_back(ms);
+  }
+  return out;
+}
+
+void events_destroy(std::vector<int64_t> handles) {
+  for (auto h : handles) cudaEventDestroy(reinterpret_cast<cudaEvent_t>(h));
+}
+
 int64_t device_error() {
   int32_t code = 0;
   check_status(lsek_device_error(&code, static_cast<void*>(at::cuda::getCurrentCUDAStream().stream())));
@@ -420,6 +452,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("renormalize"), py::arg("scoring_func"), py::arg("swiglu_limit"),
         py::arg("workspace"), py::arg("topk_weights") = py::none(),
         py::arg("topk_indices") = py::none(), py::arg("stage_events") = std::vector<int64_t>{});
+  m.def("events_create", &events_create, py::arg("n"));
+  m.def("events_elapsed_ms", &events_elapsed_ms, py::arg("handles"));
+  m.def("events_destroy", &events_destroy, py::arg("handles"));
   m.def("device_error", &device_error,
         "Reads and clears the device-side error word (synchronises the current stream).");
   m.def("version", [] { return std::string(lsek_version()); });

@@ -48,6 +48,22 @@ def moe_layer_forward(hidden: torch.Tensor, logits: torch.Tensor, bias: Optional
 STAGES = ("gating", "route", "row_copy", "gate_up_swiglu_gemm", "down_gemm", "unpermute")
 
 
+class StageEvents:
+    """len(STAGES) + 1 timing events that lsek_moe_layer_forward records
+    between its stages; elapsed_ms() gives the per-stage milliseconds."""
+
+    def __init__(self):
+        self.handles = _C.events_create(len(STAGES) + 1)
+
+    def elapsed_ms(self) -> dict:
+        return dict(zip(STAGES, _C.events_elapsed_ms(self.handles)))
+
+    def __del__(self):
+        if getattr(self, "handles", None):
+            _C.events_destroy(self.handles)
+            self.handles = []
+
+
 class MoELayer:
     """A routed-expert layer with resident weights and a reusable workspace.
 
@@ -89,14 +105,14 @@ class MoELayer:
                 out: Optional[torch.Tensor] = None,
                 topk_weights: Optional[torch.Tensor] = None,
                 topk_indices: Optional[torch.Tensor] = None,
-                stage_events: Optional[list] = None) -> torch.Tensor:
-        """stage_events: None or STAGES + 1 torch.cuda.Event(enable_timing=True),
-        recorded on the current stream around the six stages (gating, route,
-        row copy, gate/up GEMM + SwiGLU, down GEMM, unpermute)."""
+                stage_events: Optional["StageEvents"] = None) -> torch.Tensor:
+        """stage_events: None or a StageEvents, recorded on the current
+        stream around the six stages (gating, route, row copy, gate/up GEMM +
+        SwiGLU, down GEMM, unpermute)."""
         self._ensure_workspace(hidden.shape[0])
         if out is None:
             out = torch.empty_like(hidden)
-        handles = [] if stage_events is None else [e.cuda_event for e in stage_events]
+        handles = [] if stage_events is None else stage_events.handles
         _C.moe_layer_forward_out(out, hidden, logits, self.bias, self.w_gu, self.w_down,
                                  self.topk, self.n_group, self.topk_group,
                                  self.routed_scaling_factor, self.renormalize, self.scoring_func,
