@@ -136,6 +136,35 @@ LSEK_API lsek_status lsek_moe_permute(void* permuted_input, int32_t* expert_offs
                              void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* Size of the fixed device buffer behind lsek_moe_permute_noalloc (1 MiB). */
+#define LSEK_NOALLOC_PERMUTE_SCRATCH_BYTES (1u << 20)
+
+/* lsek_moe_permute without a workspace argument and without allocating.
+ * No counterpart in the reference: it exists for callers that cannot
+ * allocate device memory around this call, such as plugin hosts that are
+ * handed their input and output buffers by another runtime and own no
+ * allocator, or runtimes that plan all device memory at start-up and treat
+ * any later cudaMalloc as an error.
+ * Same arguments, results and limits as lsek_moe_permute.  Its scratch is a
+ * static 1 MiB device buffer inside liblsek (one per GPU that loads the
+ * library, held until the process exits), which bounds the problem size:
+ * ceil(num_tokens * topk / 4096) * (num_experts + 1) * 4 bytes must not
+ * exceed LSEK_NOALLOC_PERMUTE_SCRATCH_BYTES (with 256 experts: up to about
+ * 4.1 M slots, e.g. 524288 tokens at top-8); larger requests return
+ * LSEK_ERR_INVALID_ARG without launching anything.  The first call on a
+ * device looks up the buffer's device address with that device current;
+ * make that first call before any stream capture on the device.  Every call
+ * reuses the same buffer and needs nothing in it cleared (each call's count
+ * pass overwrites every entry its later passes read), but two calls that
+ * overlap on the GPU, e.g. on two streams, race on it. */
+LSEK_API lsek_status lsek_moe_permute_noalloc(void* permuted_input, int32_t* expert_offsets,
+                                     int32_t* src_to_dest_map, int32_t* permuted_idx,
+                                     const void* hidden_states,
+                                     const int32_t* topk_indices, int32_t num_tokens,
+                                     int32_t topk, int32_t hidden_dim,
+                                     int32_t num_experts, int32_t elem_size_bytes,
+                                     void* stream);
+
 /* Weighted unpermute.  fp32_output == 0: out [T,H] (dtype) =
  * round(sum_k fma(w[t,k], x[s2d[t,k]], acc)), fp32 accumulation in slot order.
  * fp32_output != 0: out is f32 [T,topk,H], out[t,k,:] = w[t,k]*x[s2d[t,k]]

@@ -33,6 +33,8 @@
 //             (moe_permute.cu:330-434)
 //   reduce    out[t] = bf16(((0 + in_0) + in_1) + ...) in fp32
 //             (moe_permute.cu:440-474)
+#include <mutex>
+
 #include "common.cuh"
 
 namespace lsek {
@@ -569,6 +571,40 @@ using namespace lsek;
 
 static bool dtype_16bit(int32_t dt) { return dt == LSEK_BF16 || dt == LSEK_FP16; }
 
+// ---- allocation-free permute ------------------------------------------------------------
+//
+// Scratch of lsek_moe_permute_noalloc: the per-chunk expert counts of the
+// multi-CTA route, in a fixed device array instead of a caller workspace.
+// The array exists once per GPU that loads this library and lives until
+// the process exits.  Host code must not hand `g_noalloc_scratch` itself to
+// a kernel: on the host that name is only a stand-in for the symbol, so its
+// device address is looked up with cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) int32_t g_noalloc_scratch[LSEK_NOALLOC_PERMUTE_SCRATCH_BYTES / 4];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::once_flag g_noalloc_once[kMaxDevices];
+void* g_noalloc_ptr[kMaxDevices];
+cudaError_t g_noalloc_err[kMaxDevices];
+
+// Device address of g_noalloc_scratch on the current device; the first call
+// per device performs the lookup with that device current.
+lsek_status noalloc_scratch(void** out) {
+  int dev = 0;
+  LSEK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(LSEK_ERR_UNSUPPORTED, "moe_permute_noalloc: device ordinal %d out of range", dev);
+  std::call_once(g_noalloc_once[dev], [dev] {
+    g_noalloc_err[dev] = cudaGetSymbolAddress(&g_noalloc_ptr[dev], g_noalloc_scratch);
+  });
+  if (g_noalloc_err[dev] != cudaSuccess)
+    return fail(LSEK_ERR_CUDA, "moe_permute_noalloc: cudaGetSymbolAddress failed: %s",
+                cudaGetErrorString(g_noalloc_err[dev]));
+  *out = g_noalloc_ptr[dev];
+  return LSEK_OK;
+}
+}  // namespace
+
 extern "C" size_t lsek_moe_permute_workspace_size(int32_t max_tokens, int32_t max_topk,
                                                   int32_t num_experts) {
   if (max_tokens < 0 || max_topk < 0 || num_experts < 0) return 0;
@@ -610,6 +646,33 @@ extern "C" lsek_status lsek_moe_permute(void* permuted_input, int32_t* expert_of
   if (hidden_dim == 0) return LSEK_OK;
   return launch_permute_rows(permuted_input, hidden_states, src_to_dest_map, num_tokens, topk,
                              static_cast<int64_t>(hidden_dim) * elem_size_bytes, st);
+}
+
+extern "C" lsek_status lsek_moe_permute_noalloc(void* permuted_input, int32_t* expert_offsets,
+                                                int32_t* src_to_dest_map, int32_t* permuted_idx,
+                                                const void* hidden_states,
+                                                const int32_t* topk_indices, int32_t num_tokens,
+                                                int32_t topk, int32_t hidden_dim,
+                                                int32_t num_experts, int32_t elem_size_bytes,
+                                                void* stream) {
+  LSEK_REQUIRE(num_tokens >= 0 && topk >= 0 && hidden_dim >= 0,
+               "moe_permute_noalloc: sizes must be >= 0");
+  LSEK_REQUIRE(num_experts >= 1, "moe_permute_noalloc: num_experts must be >= 1");
+  if (num_experts > 1023)
+    return fail(LSEK_ERR_UNSUPPORTED, "moe_permute_noalloc: num_experts must be <= 1023");
+  const int64_t n = static_cast<int64_t>(num_tokens) * topk;
+  const size_t need = permute_workspace_bytes(n, num_experts);
+  LSEK_REQUIRE(need <= LSEK_NOALLOC_PERMUTE_SCRATCH_BYTES,
+               "moe_permute_noalloc: %lld slots over %d experts need %zu bytes of scratch, more "
+               "than the %u-byte static buffer; call lsek_moe_permute with a workspace instead",
+               static_cast<long long>(n), num_experts, need,
+               static_cast<unsigned>(LSEK_NOALLOC_PERMUTE_SCRATCH_BYTES));
+  void* scratch = nullptr;
+  const lsek_status s = noalloc_scratch(&scratch);
+  if (s != LSEK_OK) return s;
+  return lsek_moe_permute(permuted_input, expert_offsets, src_to_dest_map, permuted_idx,
+                          hidden_states, topk_indices, num_tokens, topk, hidden_dim, num_experts,
+                          elem_size_bytes, scratch, LSEK_NOALLOC_PERMUTE_SCRATCH_BYTES, stream);
 }
 
 extern "C" lsek_status lsek_moe_unpermute(void* output, const void* permuted_output,
