@@ -148,9 +148,9 @@ LSEK_API lsek_status lsek_moe_permute(void* permuted_input, int32_t* expert_offs
  * Same arguments, results and limits as lsek_moe_permute.  Its scratch is a
  * static 1 MiB device buffer inside liblsek (one per GPU that loads the
  * library, held until the process exits), which bounds the problem size:
- * ceil(num_tokens * topk / 4096) * (num_experts + 1) * 4 bytes must not
+ * ceil(num_tokens * topk / 2048) * (num_experts + 1) * 4 bytes must not
  * exceed LSEK_NOALLOC_PERMUTE_SCRATCH_BYTES (with 256 experts: up to about
- * 4.1 M slots, e.g. 524288 tokens at top-8); larger requests return
+ * 2.09 M slots, e.g. 261120 tokens at top-8); larger requests return
  * LSEK_ERR_INVALID_ARG without launching anything.  The first call on a
  * device looks up the buffer's device address with that device current;
  * make that first call before any stream capture on the device.  Every call
@@ -213,18 +213,26 @@ LSEK_API lsek_status lsek_fused_swiglu(void* output, const void* input,
 
 /* ---- expert contraction (tcgen05 / TMEM / TMA) -------------------------- */
 
+/* Scratch for the grouped GEMMs' work-unit counter.  With it the persistent
+ * CTAs take work units dynamically, which keeps the CTAs that share a weight
+ * tile in step (L2 reuse); with workspace == NULL they take a static stride.
+ * The entry point zeroes the counter on the stream before the launch. */
+#define LSEK_GEMM_WORKSPACE_BYTES 256
+
 /* Grouped bf16 GEMM over experts: for each expert e,
  *   D[r, :] = A[r, :] . B[e]^T   for r in [offsets[e], offsets[e+1])
  * A [rows, K] bf16 row-major, B [E, N, K] bf16 (row-major per expert),
  * D [rows, N] bf16, fp32 accumulation.  Rows outside every expert range are
  * not written.  K % 8 == 0, N % 32 == 0, A/B/D 16-byte aligned.
+ * workspace: NULL or LSEK_GEMM_WORKSPACE_BYTES of device scratch (see above).
  * The reference documents this contraction (USAGE.md:40-57) and tests it
  * with ref_grouped_gemm (tests/test_reference.py:228-254) but ships the
  * kernel in a separate library; argument order follows USAGE.md:122-126. */
 LSEK_API lsek_status lsek_grouped_gemm_bf16(void* D, const void* A, const void* B,
                                    const int32_t* expert_offsets,
                                    int32_t num_experts, int32_t rows,
-                                   int32_t N, int32_t K, void* stream);
+                                   int32_t N, int32_t K, void* workspace,
+                                   size_t workspace_bytes, void* stream);
 
 /* Gate/up grouped GEMM with the SwiGLU in its epilogue.  W_gu [E, 2I, K]
  * holds gate rows 0..I-1 and up rows I..2I-1 per expert.  For each row r of
@@ -237,7 +245,8 @@ LSEK_API lsek_status lsek_grouped_gemm_swiglu_bf16(void* Hout, const void* A,
                                           const int32_t* expert_offsets,
                                           int32_t num_experts, int32_t rows,
                                           int32_t I, int32_t K,
-                                          float swiglu_limit, void* stream);
+                                          float swiglu_limit, void* workspace,
+                                          size_t workspace_bytes, void* stream);
 
 /* ---- whole MoE layer ------------------------------------------------------ */
 

@@ -54,13 +54,25 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Merges another lane's (top1, top2) into ours; the result is the top-2 of
+// the union as a multiset (the pair logic of grouped_topk_kernel,
+// sm120/gating/topk_gating.cu:289-300).
+__device__ __forceinline__ void merge_top2(float& t1, float& t2, float o1, float o2) {
+  if (t1 >= o1) {
+    t2 = (t2 >= o1) ? t2 : o1;
+  } else {
+    t2 = (o2 >= t1) ? o2 : t1;
+    t1 = o1;
+  }
+}
+
 template <int EPL>
-__global__ void __launch_bounds__(256) topk_gating_kernel(
+__global__ void __launch_bounds__(256, 3) topk_gating_kernel(
     float* __restrict__ out_w, int32_t* __restrict__ out_i,
     const float* __restrict__ logits, const float* __restrict__ bias, int T,
     int E, int topk, int n_group, int topk_group, float rsf, int renorm,
-    int scoring, int vec_ok) {
-  extern __shared__ float s_group[];  // per warp: sel values, padded 33/32
+    int scoring, int vec_ok, int seg_lanes) {
+  extern __shared__ float s_group[];  // per warp: sel values, padded 33/32 (general path)
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int warps_per_block = blockDim.x >> 5;
@@ -68,14 +80,6 @@ __global__ void __launch_bounds__(256) topk_gating_kernel(
   float* s_sel = s_group + warp * pad_stride;
   const int e0 = lane * EPL;
   const int epg = E / n_group;
-
-  // Bias is the same for every token: keep this lane's slice in registers.
-  float b[EPL];
-#pragma unroll
-  for (int j = 0; j < EPL; ++j) {
-    const int e = e0 + j;
-    b[j] = (bias != nullptr && e < E) ? bias[e] : 0.0f;
-  }
 
   for (int t = blockIdx.x * warps_per_block + warp; t < T;
        t += gridDim.x * warps_per_block) {
@@ -92,49 +96,76 @@ __global__ void __launch_bounds__(256) topk_gating_kernel(
       for (int j = 0; j < EPL; ++j) x[j] = (e0 + j < E) ? __ldg(row + e0 + j) : 0.0f;
     }
 
+    // x[] becomes the biased selection score; sc[] keeps the unbiased score.
     float sc[EPL];
-    uint32_t key[EPL];
 #pragma unroll
     for (int j = 0; j < EPL; ++j) {
       const int e = e0 + j;
       const float s = scoring == LSEK_SCORING_SIGMOID ? score_sigmoid(x[j])
                                                       : score_sqrtsoftplus(x[j]);
-      const float sel = (bias != nullptr) ? __fadd_rn(s, b[j]) : s;
       sc[j] = s;
-      key[j] = (e < E) ? order_key(sel) : 0u;
-      if (n_group > 1 && e < E) s_sel[e + (e >> 5)] = sel;
+      x[j] = (e >= E) ? -INFINITY : (bias != nullptr ? __fadd_rn(s, __ldg(bias + e)) : s);
     }
+    uint32_t key[EPL];
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) key[j] = (e0 + j < E) ? order_key(x[j]) : 0u;
 
     if (n_group > 1) {
-      __syncwarp();
-      float gscore = 0.0f;
-      if (lane < n_group) {
-        float top1 = -INFINITY, top2 = -INFINITY;
-        const int gb = lane * epg;
-        for (int i = 0; i < epg; ++i) {
-          const int e = gb + i;
-          const float v = s_sel[e + (e >> 5)];
-          if (v > top1) {
-            top2 = top1;
-            top1 = v;
-          } else if (v > top2) {
-            top2 = v;
-          }
-        }
-        gscore = (epg >= 2) ? __fadd_rn(top1, top2) : top1;
-      }
-      int rank = 0;
-      for (int h = 0; h < n_group; ++h) {
-        const float o = __shfl_sync(kFull, gscore, h);
-        rank += (o > gscore) || (o == gscore && h < lane);
-      }
-      const unsigned kept = __ballot_sync(kFull, lane < n_group && rank < topk_group);
+      bool kept_mine[EPL];
+      if (seg_lanes > 0) {
+        // Each lane's experts lie in one group and a group spans seg_lanes
+        // aligned lanes: top-2 by xor-shuffles inside the segment.
+        float t1 = -INFINITY, t2 = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < EPL; ++j) {
-        const int e = e0 + j;
-        if (e < E && !((kept >> (e / epg)) & 1u)) key[j] = 0u;
+        for (int j = 0; j < EPL; ++j) merge_top2(t1, t2, x[j], -INFINITY);
+        for (int off = 1; off < seg_lanes; off <<= 1) {
+          const float o1 = __shfl_xor_sync(kFull, t1, off);
+          const float o2 = __shfl_xor_sync(kFull, t2, off);
+          merge_top2(t1, t2, o1, o2);
+        }
+        const float mine = (epg >= 2) ? __fadd_rn(t1, t2) : t1;
+        const int g_me = lane / seg_lanes;
+        int rank = 0;
+        for (int h = 0; h < n_group; ++h) {
+          const float o = __shfl_sync(kFull, mine, h * seg_lanes);
+          rank += (o > mine) || (o == mine && h < g_me);
+        }
+#pragma unroll
+        for (int j = 0; j < EPL; ++j) kept_mine[j] = rank < topk_group;
+      } else {
+        // General layout: per-group scan through shared memory.
+#pragma unroll
+        for (int j = 0; j < EPL; ++j) {
+          const int e = e0 + j;
+          if (e < E) s_sel[e + (e >> 5)] = x[j];
+        }
+        __syncwarp();
+        float gscore = 0.0f;
+        if (lane < n_group) {
+          float t1 = -INFINITY, t2 = -INFINITY;
+          const int gb = lane * epg;
+          for (int i = 0; i < epg; ++i) {
+            const int e = gb + i;
+            merge_top2(t1, t2, s_sel[e + (e >> 5)], -INFINITY);
+          }
+          gscore = (epg >= 2) ? __fadd_rn(t1, t2) : t1;
+        }
+        int rank = 0;
+        for (int h = 0; h < n_group; ++h) {
+          const float o = __shfl_sync(kFull, gscore, h);
+          rank += (o > gscore) || (o == gscore && h < lane);
+        }
+        const unsigned kept = __ballot_sync(kFull, lane < n_group && rank < topk_group);
+#pragma unroll
+        for (int j = 0; j < EPL; ++j) {
+          const int e = e0 + j;
+          kept_mine[j] = e < E && ((kept >> (e / epg)) & 1u);
+        }
+        __syncwarp();  // s_sel is rewritten by the next token
       }
-      __syncwarp();  // s_sel is rewritten by the next token
+#pragma unroll
+      for (int j = 0; j < EPL; ++j)
+        if (!kept_mine[j]) key[j] = 0u;
     }
 
     // Local best: highest key, lowest j on ties (lowest expert id).
@@ -189,15 +220,25 @@ cudaError_t launch_topk(float* w, int32_t* idx, const float* logits,
                         int vec_ok, cudaStream_t st) {
   const int threads = 256;
   const int warps = threads / 32;
+  // Register path for groups: every lane's EPL experts in one group and a
+  // group spanning a power-of-two number of whole lanes.
+  int seg = 0;
+  if (p.n_group > 1) {
+    const int epg = p.num_experts / p.n_group;
+    const int lanes = epg / EPL;
+    if (p.num_experts == 32 * EPL && epg % EPL == 0 && lanes >= 1 && (lanes & (lanes - 1)) == 0)
+      seg = lanes;
+  }
   const size_t smem =
-      p.n_group > 1 ? static_cast<size_t>(warps) * (p.num_experts + (p.num_experts >> 5) + 1) * sizeof(float)
-                    : 0;
+      (p.n_group > 1 && seg == 0)
+          ? static_cast<size_t>(warps) * (p.num_experts + (p.num_experts >> 5) + 1) * sizeof(float)
+          : 0;
   const int blocks_needed = static_cast<int>(ceil_div(p.num_tokens, warps));
-  const int grid = blocks_needed < num_sms() * 8 ? blocks_needed : num_sms() * 8;
+  const int grid = blocks_needed < num_sms() * 3 ? blocks_needed : num_sms() * 3;
   topk_gating_kernel<EPL><<<grid, threads, smem, st>>>(
       w, idx, logits, bias, p.num_tokens, p.num_experts, p.topk,
       p.n_group > 1 ? p.n_group : 1, p.topk_group, p.routed_scaling_factor,
-      p.renormalize, p.scoring_func, vec_ok);
+      p.renormalize, p.scoring_func, vec_ok, seg);
   return cudaGetLastError();
 }
 

@@ -11,13 +11,19 @@
 // share one weight tile are taken by neighbouring CTAs at the same time and
 // the weight tile is read from HBM once (the second read hits L2); the 16-28
 // n-tiles of one expert reuse its A rows from L2.  A persistent grid of one
-// CTA per SM walks the unit list with a static stride.  At DeepSeek-V3 shape
-// the kernel is bound by streaming the 22.5 GB of weights from HBM.
+// CTA per SM takes units from an atomic counter in caller scratch (or, with
+// no scratch, with a static stride): CTAs that become free together take
+// neighbouring units, so the two m-tiles of an expert read each weight line
+// within microseconds of each other and the second read hits L2, where a
+// static stride lets the CTAs drift apart until the line has been evicted.
+// At DeepSeek-V3 shape the kernel is bound by streaming the weights from HBM.
 //
 // One CTA = 6 warps:
-//   warp 0      TMA producer: per k-block loads A [128 x 64] and two B boxes
-//               [128 x 64] into a 4-stage ring (128-byte swizzle), completing
-//               on the stage's `full` mbarrier.
+//   warp 0      TMA producer: takes the next unit id, publishes it to the
+//               other warps through a 4-entry shared-memory queue, then per
+//               k-block loads A [128 x 64] and two B boxes [128 x 64] into a
+//               4-stage ring (128-byte swizzle), completing on the stage's
+//               `full` mbarrier.
 //   warp 1      MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=16) per stage into
 //               one of two TMEM accumulators (2 x 256 fp32 columns = all 512
 //               columns); tcgen05.commit frees the stage and, after the last
@@ -26,6 +32,13 @@
 //               lanes 32*(w%4)..+31 = its 32 rows), convert, store to global,
 //               then release the accumulator; it overlaps the next tile's
 //               main loop thanks to the second accumulator.
+// Small tiles (at most kSwapMaxRows valid rows: the tail of an expert with
+// 129..192 rows, or every tile at decode sizes) swap the operands: the two
+// weight boxes become the MMA's M side (2 x M=128) and the tile's r token
+// rows its N side (N = r rounded up to 16), so the tensor-core work scales
+// with r instead of a full 128-row tile.  The epilogue of such a tile reads
+// the transposed accumulator (TMEM lane = output column, TMEM column =
+// token).  The same products are summed in the same k order either way.
 // SWIGLU mode stacks 128 gate rows (rows n*128 of the expert) and the matching
 // 128 up rows (rows I + n*128) as the two B boxes, so one N=256 MMA yields g
 // and u for 128 output columns; the epilogue rounds both to bf16 and applies
@@ -65,6 +78,8 @@ constexpr int kStageBytes = kABytes + 2 * kBoxBytes;  // 48 KB
 constexpr int kTmemCols = 2 * kBN;             // two accumulators
 constexpr int kThreads = 192;
 constexpr int kMaxExperts = 1024;
+constexpr int kUnitQ = 4;                      // unit ids in flight between warps
+constexpr int kSwapMaxRows = 64;               // tiles this small use swapped operands
 
 // M=128, N=256, A/B bf16 K-major, D fp32 (tcgen05 instruction descriptor:
 // D format bits 4-5, A format bits 7-9, B format bits 10-12, N>>3 bits 17-22,
@@ -87,6 +102,7 @@ struct Params {
   int out_tile_cols;       // output columns per tile
   int n_out;               // output width
   float swiglu_limit;
+  int32_t* counter;        // zeroed unit counter in device memory, or null (static stride)
 };
 
 struct Smem {
@@ -96,6 +112,9 @@ struct Smem {
   uint64_t acc_full_bar[2];
   uint64_t acc_empty_bar[2];
   uint64_t mma_done_bar;
+  uint64_t q_full[kUnitQ];
+  uint64_t q_empty[kUnitQ];
+  int32_t unit_q[kUnitQ];
   uint32_t tmem_base;
   int32_t abort;
   int32_t warp_tot[kThreads / 32];
@@ -206,6 +225,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+      " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -221,6 +249,18 @@ __device__ __forceinline__ float round_bf16(float x) {
 __device__ __forceinline__ int mtiles_of(const Smem& s, int e) {
   const int n = s.offs[e + 1] - s.offs[e];
   return n > 0 ? (n + kBM - 1) / kBM : 0;
+}
+
+// Valid rows of m-tile m of expert e (1..kBM).
+__device__ __forceinline__ int tile_rows(const Smem& s, int e, int m) {
+  const int left = s.offs[e + 1] - s.offs[e] - m * kBM;
+  return left < kBM ? left : kBM;
+}
+
+// Instruction descriptor of a swapped tile: M=128 weight rows, N=nn tokens.
+__device__ __forceinline__ uint32_t swap_idesc(int nn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(nn >> 3) << 17) |
+         (static_cast<uint32_t>(kBM >> 4) << 24);
 }
 
 // Maps a unit id to (expert, m-tile, n-tile): the largest e with cum[e] <= id
@@ -293,6 +333,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.acc_empty_bar[i], 4);
     }
     mbar_init(&s.mma_done_bar, 1);
+    for (int i = 0; i < kUnitQ; ++i) {
+      mbar_init(&s.q_full[i], 1);
+      mbar_init(&s.q_empty[i], 1 + 4);  // MMA lane + four epilogue warps
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
@@ -322,7 +366,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t issued = 0;
       uint32_t last_phase[kStages] = {0, 0, 0, 0};
       bool ok = true;
-      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x) {
+      int qslot = 0;
+      uint32_t qphase = 0;
+      for (int i = 0; ok; ++i) {
+        if (!mbar_wait(&s.q_empty[qslot], qphase ^ 1u, abort, kDevErrGemmProducerWait, true)) {
+          ok = false;
+          break;
+        }
+        int unit = p.counter ? atomicAdd(p.counter, 1) : blockIdx.x + i * static_cast<int>(gridDim.x);
+        if (unit >= total) unit = -1;
+        s.unit_q[qslot] = unit;
+        mbar_arrive(&s.q_full[qslot]);
+        if (++qslot == kUnitQ) {
+          qslot = 0;
+          qphase ^= 1u;
+        }
+        if (unit < 0) break;
         int e, m, n;
         decode_unit(s, E, unit, e, m, n);
         const int row0 = s.offs[e] + m * kBM;
@@ -358,8 +417,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int it = 0;
-      for (int unit = blockIdx.x; unit < total && ok; unit += gridDim.x, ++it) {
+      int qslot = 0;
+      uint32_t qphase = 0;
+      for (int it = 0; ok; ++it) {
+        if (!mbar_wait(&s.q_full[qslot], qphase, abort, kDevErrGemmMmaWait, true)) break;
+        const int unit = s.unit_q[qslot];
+        mbar_arrive(&s.q_empty[qslot]);
+        if (++qslot == kUnitQ) {
+          qslot = 0;
+          qphase ^= 1u;
+        }
+        if (unit < 0) break;
+        int e, m, n;
+        decode_unit(s, E, unit, e, m, n);
+        const int rows_here = tile_rows(s, e, m);
+        const bool swapped = rows_here <= kSwapMaxRows;
+        const int nn = (rows_here + 15) & ~15;
+        const uint32_t sw_idesc = swap_idesc(nn);
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&s.acc_empty_bar[acc], acc_phase ^ 1u, abort, kDevErrGemmMmaWait, true)) {
@@ -376,10 +450,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(s.tiles[stage]);
           const uint32_t b_addr = a_addr + kABytes;
+          if (swapped) {
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_bf16(d_tmem, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
-                      kIdesc, (kb | kk) != 0 ? 1u : 0u);
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t tok = smem_desc_sw128(a_addr + kk * 32);
+              const uint32_t acc_in = (kb | kk) != 0 ? 1u : 0u;
+              umma_bf16(d_tmem, smem_desc_sw128(b_addr + kk * 32), tok, sw_idesc, acc_in);
+              umma_bf16(d_tmem + static_cast<uint32_t>(nn),
+                        smem_desc_sw128(b_addr + kBoxBytes + kk * 32), tok, sw_idesc, acc_in);
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_bf16(d_tmem, smem_desc_sw128(a_addr + kk * 32),
+                        smem_desc_sw128(b_addr + kk * 32), kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          }
           umma_commit(&s.empty_bar[stage]);
           if (++stage == kStages) {
             stage = 0;
@@ -395,22 +480,64 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ===================== epilogue (warps 2..5) =====================
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    int it = 0;
-    for (int unit = blockIdx.x; unit < total; unit += gridDim.x, ++it) {
+    int qslot = 0;
+    uint32_t qphase = 0;
+    for (int it = 0;; ++it) {
+      if (!mbar_wait(&s.q_full[qslot], qphase, abort, kDevErrGemmEpilogueWait, true)) break;
+      const int unit = s.unit_q[qslot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.q_empty[qslot]);
+      if (++qslot == kUnitQ) {
+        qslot = 0;
+        qphase ^= 1u;
+      }
+      if (unit < 0) break;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(&s.acc_full_bar[acc], acc_phase, abort, kDevErrGemmEpilogueWait, true)) break;
       tc_fence_after();
       int e, m, n;
       decode_unit(s, E, unit, e, m, n);
-      const int r = s.offs[e] + m * kBM + q * 32 + lane;
+      const int rows_here = tile_rows(s, e, m);
+      const int row0 = s.offs[e] + m * kBM;
+      const int r = row0 + q * 32 + lane;
       const bool valid = r < s.offs[e + 1];
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kBN);
       const int col0 = n * p.out_tile_cols;
       const int cols_here = min(p.out_tile_cols, p.n_out - col0);
       __nv_bfloat16* drow = p.D + static_cast<int64_t>(valid ? r : 0) * p.ldd + col0;
-      if (SWIGLU) {
+      if (rows_here <= kSwapMaxRows) {
+        // Transposed accumulator: this thread's TMEM lane is weight row
+        // w = 32q + lane of each box, columns [0, nn) hold box 0 for the
+        // tile's tokens and [nn, 2nn) box 1.
+        const int nn = (rows_here + 15) & ~15;
+        const int w = q * 32 + lane;
+        __nv_bfloat16* dcol = p.D + static_cast<int64_t>(row0) * p.ldd + col0;
+#pragma unroll 1
+        for (int t0 = 0; t0 < nn; t0 += 16) {
+          uint32_t v0[16], v1[16];
+          tmem_ld16(tbase + t0, v0);
+          tmem_ld16(tbase + nn + t0, v1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int t = t0 + i;
+            if (t >= rows_here) break;
+            __nv_bfloat16* dst = dcol + static_cast<int64_t>(t) * p.ldd;
+            if (SWIGLU) {
+              if (w < cols_here)
+                dst[w] = __float2bfloat16_rn(swiglu_f32(round_bf16(__uint_as_float(v0[i])),
+                                                        round_bf16(__uint_as_float(v1[i])),
+                                                        p.swiglu_limit));
+            } else {
+              if (w < cols_here) dst[w] = __float2bfloat16_rn(__uint_as_float(v0[i]));
+              if (kBoxRows + w < cols_here)
+                dst[kBoxRows + w] = __float2bfloat16_rn(__uint_as_float(v1[i]));
+            }
+          }
+        }
+      } else if (SWIGLU) {
 #pragma unroll 1
         for (int c = 0; c < kBoxRows; c += 32) {
           uint32_t g[32], u[32];
@@ -511,7 +638,7 @@ lsek_status make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_
 
 template <bool SWIGLU>
 lsek_status launch(void* D, const void* A, const void* B, const int32_t* offsets, int E, int rows,
-                   int n_out, int b_rows, int K, float limit, cudaStream_t st) {
+                   int n_out, int b_rows, int K, float limit, int32_t* counter, cudaStream_t st) {
   static PerDeviceOnce attrs;
   const cudaError_t ae = once_per_device(attrs, [] {
     return cudaFuncSetAttribute(grouped_gemm_kernel<SWIGLU>,
@@ -534,6 +661,8 @@ lsek_status launch(void* D, const void* A, const void* B, const int32_t* offsets
   p.n_out = n_out;
   p.b_rows = b_rows;
   p.swiglu_limit = limit;
+  p.counter = counter;
+  if (counter != nullptr) LSEK_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(int32_t), st));
   if (SWIGLU) {
     p.n_tiles = static_cast<int>(ceil_div(n_out, kBoxRows));
     p.b_tile_rows = kBoxRows;
@@ -569,16 +698,18 @@ lsek_status validate(const char* name, const void* D, const void* A, const void*
 
 }  // namespace gemm
 
-// Used by the layer forward.
+// Used by the layer forward.  `counter` is one zero-able int32 of device
+// scratch for dynamic unit scheduling, or null for the static stride.
 lsek_status grouped_gemm_plain(void* D, const void* A, const void* B, const int32_t* offsets, int E,
-                               int rows, int N, int K, cudaStream_t st) {
+                               int rows, int N, int K, int32_t* counter, cudaStream_t st) {
   if (rows == 0 || N == 0) return LSEK_OK;
-  return gemm::launch<false>(D, A, B, offsets, E, rows, N, N, K, 0.0f, st);
+  return gemm::launch<false>(D, A, B, offsets, E, rows, N, N, K, 0.0f, counter, st);
 }
 lsek_status grouped_gemm_swiglu(void* H, const void* A, const void* Wgu, const int32_t* offsets,
-                                int E, int rows, int I, int K, float limit, cudaStream_t st) {
+                                int E, int rows, int I, int K, float limit, int32_t* counter,
+                                cudaStream_t st) {
   if (rows == 0 || I == 0) return LSEK_OK;
-  return gemm::launch<true>(H, A, Wgu, offsets, E, rows, I, 2 * I, K, limit, st);
+  return gemm::launch<true>(H, A, Wgu, offsets, E, rows, I, 2 * I, K, limit, counter, st);
 }
 
 }  // namespace lsek
@@ -594,22 +725,32 @@ extern "C" lsek_status lsek_device_error(int32_t* code, void* stream) {
   return LSEK_OK;
 }
 
+static int32_t* gemm_counter(void* workspace, size_t workspace_bytes) {
+  return (workspace != nullptr && workspace_bytes >= sizeof(int32_t)) ? static_cast<int32_t*>(workspace)
+                                                                      : nullptr;
+}
+
 extern "C" lsek_status lsek_grouped_gemm_bf16(void* D, const void* A, const void* B,
                                               const int32_t* expert_offsets, int32_t num_experts,
-                                              int32_t rows, int32_t N, int32_t K, void* stream) {
+                                              int32_t rows, int32_t N, int32_t K, void* workspace,
+                                              size_t workspace_bytes, void* stream) {
   using namespace lsek;
   lsek_status s = gemm::validate("grouped_gemm_bf16", D, A, B, expert_offsets, num_experts, rows, N, K);
   if (s != LSEK_OK) return s;
   LSEK_REQUIRE(static_cast<int64_t>(num_experts) * N < (1ll << 31),
                "grouped_gemm_bf16: num_experts * N must fit in int32");
+  LSEK_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 4 == 0,
+               "grouped_gemm_bf16: workspace must be 4-byte aligned");
   return grouped_gemm_plain(D, A, B, expert_offsets, num_experts, rows, N, K,
+                            gemm_counter(workspace, workspace_bytes),
                             static_cast<cudaStream_t>(stream));
 }
 
 extern "C" lsek_status lsek_grouped_gemm_swiglu_bf16(void* Hout, const void* A, const void* W_gu,
                                                      const int32_t* expert_offsets,
                                                      int32_t num_experts, int32_t rows, int32_t I,
-                                                     int32_t K, float swiglu_limit, void* stream) {
+                                                     int32_t K, float swiglu_limit, void* workspace,
+                                                     size_t workspace_bytes, void* stream) {
   using namespace lsek;
   lsek_status s =
       gemm::validate("grouped_gemm_swiglu_bf16", Hout, A, W_gu, expert_offsets, num_experts, rows, I, K);
@@ -617,6 +758,9 @@ extern "C" lsek_status lsek_grouped_gemm_swiglu_bf16(void* Hout, const void* A, 
   LSEK_REQUIRE(swiglu_limit >= 0.0f, "grouped_gemm_swiglu_bf16: swiglu_limit must be >= 0");
   LSEK_REQUIRE(static_cast<int64_t>(num_experts) * 2 * I < (1ll << 31),
                "grouped_gemm_swiglu_bf16: num_experts * 2I must fit in int32");
+  LSEK_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 4 == 0,
+               "grouped_gemm_swiglu_bf16: workspace must be 4-byte aligned");
   return grouped_gemm_swiglu(Hout, A, W_gu, expert_offsets, num_experts, rows, I, K, swiglu_limit,
+                             gemm_counter(workspace, workspace_bytes),
                              static_cast<cudaStream_t>(stream));
 }

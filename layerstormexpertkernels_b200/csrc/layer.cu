@@ -6,7 +6,7 @@
 //
 // Workspace layout (each piece 256-byte aligned):
 //   weights f32 [T*k] | indices i32 [T*k] | offsets i32 [E+1] | s2d i32 [T*k]
-//   | perm i32 [T*k] | route scratch | X [T*k, H] bf16 (reused for the down
+//   | perm i32 [T*k] | route scratch | GEMM unit counter | X [T*k, H] bf16 (reused for the down
 //   GEMM output Y, which is written only after the gate/up GEMM has consumed
 //   X on the same stream) | Hact [T*k, I] bf16
 #include "common.cuh"
@@ -18,13 +18,14 @@ lsek_status launch_route(const int32_t* idx, int64_t n, int E, int32_t* offsets,
 lsek_status launch_permute_rows(void* dst, const void* src, const int32_t* s2d, int64_t T,
                                 int topk, int64_t row_bytes, cudaStream_t st);
 lsek_status grouped_gemm_plain(void* D, const void* A, const void* B, const int32_t* offsets,
-                               int E, int rows, int N, int K, cudaStream_t st);
+                               int E, int rows, int N, int K, int32_t* counter, cudaStream_t st);
 lsek_status grouped_gemm_swiglu(void* H, const void* A, const void* Wgu, const int32_t* offsets,
-                                int E, int rows, int I, int K, float limit, cudaStream_t st);
+                                int E, int rows, int I, int K, float limit, int32_t* counter,
+                                cudaStream_t st);
 
 namespace {
 struct LayerWs {
-  size_t w, idx, offs, s2d, perm, route, x, h, total;
+  size_t w, idx, offs, s2d, perm, route, sched, x, h, total;
 };
 size_t a256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 LayerWs layer_ws(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
@@ -37,6 +38,7 @@ LayerWs layer_ws(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
   l.s2d = o;   o += a256(n * 4);
   l.perm = o;  o += a256(n * 4);
   l.route = o; o += a256(permute_workspace_bytes(n, static_cast<int>(E)));
+  l.sched = o; o += 256;
   l.x = o;     o += a256(n * H * 2);
   l.h = o;     o += a256(n * I * 2);
   l.total = o;
@@ -87,6 +89,7 @@ extern "C" lsek_status lsek_moe_layer_forward(
   int32_t* offs = reinterpret_cast<int32_t*>(ws + l.offs);
   int32_t* s2d = reinterpret_cast<int32_t*>(ws + l.s2d);
   int32_t* perm = reinterpret_cast<int32_t*>(ws + l.perm);
+  int32_t* counter = reinterpret_cast<int32_t*>(ws + l.sched);
   void* x = ws + l.x;
   void* h = ws + l.h;
   const int64_t n = static_cast<int64_t>(T) * k;
@@ -106,10 +109,11 @@ extern "C" lsek_status lsek_moe_layer_forward(
   if (s != LSEK_OK) return s;
   if ((s = mark(3)) != LSEK_OK) return s;
   s = grouped_gemm_swiglu(h, x, W_gu, offs, E, static_cast<int>(n), inter_dim, hidden_dim,
-                          swiglu_limit, st);
+                          swiglu_limit, counter, st);
   if (s != LSEK_OK) return s;
   if ((s = mark(4)) != LSEK_OK) return s;
-  s = grouped_gemm_plain(x, h, W_down, offs, E, static_cast<int>(n), hidden_dim, inter_dim, st);
+  s = grouped_gemm_plain(x, h, W_down, offs, E, static_cast<int>(n), hidden_dim, inter_dim,
+                         counter, st);
   if (s != LSEK_OK) return s;
   if ((s = mark(5)) != LSEK_OK) return s;
   s = lsek_moe_unpermute(out, x, w, s2d, T, k, hidden_dim, LSEK_BF16, 0, stream);

@@ -5,9 +5,10 @@
 // on T*topk keys; the row copy is the HBM-bound part.
 //
 //   route   Keys are split into contiguous per-warp runs.  For each 32-key
-//           step a warp groups equal keys with __match_any_sync: a key's rank
-//           inside the step is popc(peers & lanes-below), and the lowest peer
-//           lane adds popc(peers) to the warp's running count for that expert.
+//           step a warp finds the lanes holding an equal key with one ballot
+//           per key bit (the keys need at most 11 bits): a key's rank inside
+//           the step is popc(peers & lanes-below), and the lowest peer lane
+//           adds popc(peers) to the warp's running count for that expert.
 //           Pass 1 counts, a scan over (expert, chunk, warp) turns counts into
 //           start positions, pass 2 repeats the walk and writes
 //           dest = start + rank.  Every position is fixed by the key order,
@@ -43,9 +44,9 @@ namespace {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kRouteThreads = 1024;
 constexpr int kRouteWarps = kRouteThreads / 32;
-constexpr int kSingleMaxKeys = 32768;           // keys per lane <= 32 in one CTA
-constexpr int kChunkKeyPerLane = 4;             // multi-CTA: 4 keys per lane
-constexpr int kChunkKeys = kRouteWarps * 32 * kChunkKeyPerLane;  // 4096
+constexpr int kSingleMaxKeys = 4096;            // one CTA, up to 4 keys per lane
+constexpr int kChunkKeyPerLane = 2;             // multi-CTA: 2 keys per lane
+constexpr int kChunkKeys = kRouteWarps * 32 * kChunkKeyPerLane;  // 2048
 
 __device__ __forceinline__ int clamp_key(int32_t v, int E) {
   return (v < 0 || v >= E) ? E : v;
@@ -57,24 +58,45 @@ __device__ __forceinline__ unsigned lanemask_lt() {
   return m;
 }
 
-// Loads this warp's run of keys: lane l holds keys at run_begin + i*32 + l.
+// Bits needed for every key value 0..E plus the padding key (all ones).
+__host__ __device__ __forceinline__ int key_bits(int E) {
+  int b = 1;
+  while ((1 << b) - 1 <= E) ++b;
+  return b;
+}
+
+// Loads this warp's run of keys: lane l holds keys at run_begin + i*32 + l;
+// positions past the run hold the padding key (1 << nbits) - 1.
 template <int KPL>
 __device__ __forceinline__ void load_keys(int (&key)[KPL], const int32_t* __restrict__ idx,
-                                          int run_begin, int run_end, int lane, int E) {
+                                          int run_begin, int run_end, int lane, int E,
+                                          int nbits) {
 #pragma unroll
   for (int i = 0; i < KPL; ++i) {
     const int pos = run_begin + i * 32 + lane;
-    key[i] = pos < run_end ? clamp_key(__ldg(idx + pos), E) : -1;
+    key[i] = pos < run_end ? clamp_key(__ldg(idx + pos), E) : (1 << nbits) - 1;
   }
+}
+
+// Lanes of the warp whose key equals this lane's key: one ballot per bit.
+__device__ __forceinline__ unsigned match_key(int key, int nbits) {
+  unsigned peers = kFull;
+  for (int b = 0; b < nbits; ++b) {
+    const bool bit = (key >> b) & 1;
+    const unsigned set = __ballot_sync(kFull, bit);
+    peers &= bit ? set : ~set;
+  }
+  return peers;
 }
 
 // Adds this warp's per-expert counts into cnt[0..E] (row of the warp).
 template <int KPL>
-__device__ __forceinline__ void count_keys(const int (&key)[KPL], int* cnt, int lane) {
+__device__ __forceinline__ void count_keys(const int (&key)[KPL], int* cnt, int lane, int E,
+                                           int nbits) {
 #pragma unroll
   for (int i = 0; i < KPL; ++i) {
-    const unsigned peers = __match_any_sync(kFull, key[i]);
-    if (key[i] >= 0 && lane == __ffs(peers) - 1) cnt[key[i]] += __popc(peers);
+    const unsigned peers = match_key(key[i], nbits);
+    if (key[i] <= E && lane == __ffs(peers) - 1) cnt[key[i]] += __popc(peers);
     __syncwarp();
   }
 }
@@ -82,16 +104,16 @@ __device__ __forceinline__ void count_keys(const int (&key)[KPL], int* cnt, int 
 // Assigns destinations; cnt[e] holds the warp's next free slot of expert e.
 template <int KPL>
 __device__ __forceinline__ void rank_keys(const int (&key)[KPL], int* cnt, int run_begin,
-                                          int lane, int32_t* __restrict__ s2d,
+                                          int lane, int E, int nbits, int32_t* __restrict__ s2d,
                                           int32_t* __restrict__ perm) {
   const unsigned lt = lanemask_lt();
 #pragma unroll
   for (int i = 0; i < KPL; ++i) {
-    const unsigned peers = __match_any_sync(kFull, key[i]);
+    const unsigned peers = match_key(key[i], nbits);
     int dest = 0;
-    if (key[i] >= 0) dest = cnt[key[i]] + __popc(peers & lt);
+    if (key[i] <= E) dest = cnt[key[i]] + __popc(peers & lt);
     __syncwarp();
-    if (key[i] >= 0) {
+    if (key[i] <= E) {
       if (lane == __ffs(peers) - 1) cnt[key[i]] += __popc(peers);
       const int pos = run_begin + i * 32 + lane;
       s2d[pos] = dest;
@@ -144,11 +166,12 @@ __global__ void __launch_bounds__(kRouteThreads) route_single_kernel(
   const int run = KPL * 32;
   const int rb = warp * run;
   const int re = min(n, rb + run);
+  const int nbits = key_bits(E);
   int key[KPL];
-  load_keys<KPL>(key, idx, rb, re, lane, E);
+  load_keys<KPL>(key, idx, rb, re, lane, E, nbits);
   __syncthreads();
   int* cnt = s_cnt + warp * nb;
-  count_keys<KPL>(key, cnt, lane);
+  count_keys<KPL>(key, cnt, lane, E, nbits);
   __syncthreads();
   // Exclusive prefix over warps per expert; expert totals to scan.
   const int e = threadIdx.x;
@@ -169,7 +192,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_single_kernel(
     for (int w = 0; w < kRouteWarps; ++w) s_cnt[w * nb + e] += start;
   }
   __syncthreads();
-  rank_keys<KPL>(key, cnt, rb, lane, s2d, perm);
+  rank_keys<KPL>(key, cnt, rb, lane, E, nbits, s2d, perm);
 }
 
 // Multi-CTA pass 1: per-chunk expert counts -> chunk_counts[chunk][E+1].
@@ -181,10 +204,11 @@ __global__ void __launch_bounds__(kRouteThreads) route_count_kernel(
   for (int i = threadIdx.x; i < kRouteWarps * nb; i += kRouteThreads) s_cnt[i] = 0;
   const int rb = blockIdx.x * kChunkKeys + warp * kChunkKeyPerLane * 32;
   const int re = min(n, rb + kChunkKeyPerLane * 32);
+  const int nbits = key_bits(E);
   int key[kChunkKeyPerLane];
-  load_keys<kChunkKeyPerLane>(key, idx, rb, re, lane, E);
+  load_keys<kChunkKeyPerLane>(key, idx, rb, re, lane, E, nbits);
   __syncthreads();
-  count_keys<kChunkKeyPerLane>(key, s_cnt + warp * nb, lane);
+  count_keys<kChunkKeyPerLane>(key, s_cnt + warp * nb, lane, E, nbits);
   __syncthreads();
   for (int e = threadIdx.x; e < nb; e += kRouteThreads) {
     int s = 0;
@@ -228,11 +252,12 @@ __global__ void __launch_bounds__(kRouteThreads) route_rank_kernel(
   for (int i = threadIdx.x; i < kRouteWarps * nb; i += kRouteThreads) s_cnt[i] = 0;
   const int rb = blockIdx.x * kChunkKeys + warp * kChunkKeyPerLane * 32;
   const int re = min(n, rb + kChunkKeyPerLane * 32);
+  const int nbits = key_bits(E);
   int key[kChunkKeyPerLane];
-  load_keys<kChunkKeyPerLane>(key, idx, rb, re, lane, E);
+  load_keys<kChunkKeyPerLane>(key, idx, rb, re, lane, E, nbits);
   __syncthreads();
   int* cnt = s_cnt + warp * nb;
-  count_keys<kChunkKeyPerLane>(key, cnt, lane);
+  count_keys<kChunkKeyPerLane>(key, cnt, lane, E, nbits);
   __syncthreads();
   for (int e = threadIdx.x; e < nb; e += kRouteThreads) {
     int run = chunk_start[static_cast<int64_t>(blockIdx.x) * nb + e];
@@ -243,7 +268,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_rank_kernel(
     }
   }
   __syncthreads();
-  rank_keys<kChunkKeyPerLane>(key, cnt, rb, lane, s2d, perm);
+  rank_keys<kChunkKeyPerLane>(key, cnt, rb, lane, E, nbits, s2d, perm);
 }
 
 // ---- row copy ------------------------------------------------------------------
@@ -483,10 +508,8 @@ lsek_status launch_route(const int32_t* idx, int64_t n, int E, int32_t* offsets,
       if (r != cudaSuccess) e = r;
     };
     set(reinterpret_cast<const void*>(route_single_kernel<1>));
+    set(reinterpret_cast<const void*>(route_single_kernel<2>));
     set(reinterpret_cast<const void*>(route_single_kernel<4>));
-    set(reinterpret_cast<const void*>(route_single_kernel<8>));
-    set(reinterpret_cast<const void*>(route_single_kernel<16>));
-    set(reinterpret_cast<const void*>(route_single_kernel<32>));
     set(reinterpret_cast<const void*>(route_count_kernel));
     set(reinterpret_cast<const void*>(route_rank_kernel));
     return e;
@@ -494,11 +517,9 @@ lsek_status launch_route(const int32_t* idx, int64_t n, int E, int32_t* offsets,
   if (ae != cudaSuccess) return fail(LSEK_ERR_CUDA, "moe_permute: %s", cudaGetErrorString(ae));
   if (n <= kSingleMaxKeys) {
     const int kpl = static_cast<int>(ceil_div(n, kRouteThreads));
-    if (kpl <= 1)       route_single_kernel<1><<<1, kRouteThreads, smem, st>>>(idx, static_cast<int>(n), E, offsets, s2d, perm);
-    else if (kpl <= 4)  route_single_kernel<4><<<1, kRouteThreads, smem, st>>>(idx, static_cast<int>(n), E, offsets, s2d, perm);
-    else if (kpl <= 8)  route_single_kernel<8><<<1, kRouteThreads, smem, st>>>(idx, static_cast<int>(n), E, offsets, s2d, perm);
-    else if (kpl <= 16) route_single_kernel<16><<<1, kRouteThreads, smem, st>>>(idx, static_cast<int>(n), E, offsets, s2d, perm);
-    else                route_single_kernel<32><<<1, kRouteThreads, smem, st>>>(idx, static_cast<int>(n), E, offsets, s2d, perm);
+    if (kpl <= 1)      route_single_kernel<1><<<1, kRouteThreads, smem, st>>>(idx, static_cast<int>(n), E, offsets, s2d, perm);
+    else if (kpl <= 2) route_single_kernel<2><<<1, kRouteThreads, smem, st>>>(idx, static_cast<int>(n), E, offsets, s2d, perm);
+    else               route_single_kernel<4><<<1, kRouteThreads, smem, st>>>(idx, static_cast<int>(n), E, offsets, s2d, perm);
     return check_launch("moe_permute(route)");
   }
   const int nchunks = static_cast<int>(ceil_div(n, kChunkKeys));
@@ -636,7 +657,7 @@ extern "C" lsek_status lsek_moe_permute(void* permuted_input, int32_t* expert_of
   LSEK_REQUIRE(permuted_input && src_to_dest_map && permuted_idx && hidden_states && topk_indices,
                "moe_permute: NULL tensor pointer");
   const size_t need = permute_workspace_bytes(n, num_experts);
-  if (n > 32768) {
+  if (n > kSingleMaxKeys) {
     LSEK_REQUIRE(workspace != nullptr && workspace_bytes >= need,
                  "moe_permute: workspace of %zu bytes required, got %zu", need, workspace_bytes);
   }

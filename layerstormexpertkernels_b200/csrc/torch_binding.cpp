@@ -272,10 +272,12 @@ torch::Tensor grouped_gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor 
   check_gemm_args("grouped_gemm_bf16", A, B, expert_offsets);
   const c10::cuda::OptionalCUDAGuard guard(A.device());
   auto D = torch::empty({A.size(0), B.size(1)}, A.options());
+  auto ws = torch::empty({LSEK_GEMM_WORKSPACE_BYTES}, A.options().dtype(at::kByte));
   check_status(lsek_grouped_gemm_bf16(D.data_ptr(), A.data_ptr(), B.data_ptr(),
                                       expert_offsets.data_ptr<int32_t>(), to_i32(B.size(0), "E"),
                                       to_i32(A.size(0), "rows"), to_i32(B.size(1), "N"),
-                                      to_i32(A.size(1), "K"), stream_of(A)));
+                                      to_i32(A.size(1), "K"), ws.data_ptr(),
+                                      LSEK_GEMM_WORKSPACE_BYTES, stream_of(A)));
   return D;
 }
 
@@ -286,10 +288,11 @@ torch::Tensor grouped_gemm_swiglu_bf16(torch::Tensor A, torch::Tensor W_gu,
   const c10::cuda::OptionalCUDAGuard guard(A.device());
   const int64_t I = W_gu.size(1) / 2;
   auto H = torch::empty({A.size(0), I}, A.options());
+  auto ws = torch::empty({LSEK_GEMM_WORKSPACE_BYTES}, A.options().dtype(at::kByte));
   check_status(lsek_grouped_gemm_swiglu_bf16(
       H.data_ptr(), A.data_ptr(), W_gu.data_ptr(), expert_offsets.data_ptr<int32_t>(),
       to_i32(W_gu.size(0), "E"), to_i32(A.size(0), "rows"), to_i32(I, "I"), to_i32(A.size(1), "K"),
-      static_cast<float>(swiglu_limit), stream_of(A)));
+      static_cast<float>(swiglu_limit), ws.data_ptr(), LSEK_GEMM_WORKSPACE_BYTES, stream_of(A)));
   return H;
 }
 

@@ -117,11 +117,12 @@ def test_swiglu_invalid(lib):
 
 def test_gemm_invalid(lib):
     d = ctypes.c_void_p(16)
-    assert lib.lsek_grouped_gemm_bf16(d, d, d, d, 4, 8, 64, 12, None) == LSEK_ERR_INVALID_ARG  # K % 8
-    assert lib.lsek_grouped_gemm_bf16(d, d, d, d, 4, 8, 48, 64, None) == LSEK_ERR_INVALID_ARG  # N % 32
-    assert lib.lsek_grouped_gemm_bf16(d, d, d, d, 2048, 8, 64, 64, None) == LSEK_ERR_UNSUPPORTED
+    z = ctypes.c_size_t(0)
+    assert lib.lsek_grouped_gemm_bf16(d, d, d, d, 4, 8, 64, 12, None, z, None) == LSEK_ERR_INVALID_ARG  # K % 8
+    assert lib.lsek_grouped_gemm_bf16(d, d, d, d, 4, 8, 48, 64, None, z, None) == LSEK_ERR_INVALID_ARG  # N % 32
+    assert lib.lsek_grouped_gemm_bf16(d, d, d, d, 2048, 8, 64, 64, None, z, None) == LSEK_ERR_UNSUPPORTED
     odd = ctypes.c_void_p(18)
-    assert lib.lsek_grouped_gemm_bf16(d, odd, d, d, 4, 8, 64, 64, None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_grouped_gemm_bf16(d, odd, d, d, 4, 8, 64, 64, None, z, None) == LSEK_ERR_INVALID_ARG
 
 
 def test_adaptive_invalid(lib):

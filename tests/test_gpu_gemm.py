@@ -80,7 +80,7 @@ def test_rows_outside_experts_untouched():
     lib = ctypes.CDLL(P.LIBRARY_PATH)
     st = lib.lsek_grouped_gemm_bf16(
         ctypes.c_void_p(d.data_ptr()), ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()),
-        ctypes.c_void_p(off.data_ptr()), 3, a.shape[0], 64, 128,
+        ctypes.c_void_p(off.data_ptr()), 3, a.shape[0], 64, 128, None, ctypes.c_size_t(0),
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert st == 0
     sync_and_check_device_error()
@@ -135,3 +135,34 @@ def test_empty_problem():
     b = torch.zeros(3, 64, 64, dtype=torch.bfloat16, device="cuda")
     off = torch.zeros(4, dtype=torch.int32, device="cuda")
     assert ek().grouped_gemm_bf16(a, b, off).shape == (0, 64)
+
+
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_tile_shape_does_not_change_results(swiglu):
+    """A row's output must not depend on how many other rows share its
+    expert: tiles of at most 64 rows run with swapped MMA operands, full
+    tiles without, and both must give the same bits.  Expert parallelism
+    relies on this (an expert's rows are grouped differently on each rank)."""
+    K, N = 1024, 512
+    g = torch.Generator().manual_seed(99)
+    a = torch.randn(128, K, generator=g).to(torch.bfloat16).cuda()
+    b = (torch.randn(1, N, K, generator=g) / np.sqrt(K)).to(torch.bfloat16).cuda()
+
+    def run(rows):
+        off = torch.tensor([0, rows], dtype=torch.int32, device="cuda")
+        if swiglu:
+            return ek().grouped_gemm_swiglu_bf16(a[:rows].contiguous(), b, off)
+        return ek().grouped_gemm_bf16(a[:rows].contiguous(), b, off)
+
+    full = run(128)
+    for r in (1, 15, 16, 40, 64, 65, 100):
+        assert torch.equal(run(r), full[:r]), f"rows={r}"
+    sync_and_check_device_error()
+
+
+def test_tail_tiles_of_large_experts():
+    # Experts with 129..192 rows end in a swapped tail tile.
+    a, b, off = make_problem([130, 192, 150, 129], 512, 256, seed=21)
+    out = ek().grouped_gemm_bf16(a.cuda(), b.cuda(), off.cuda())
+    sync_and_check_device_error()
+    assert_close_bf16(out, oracle_gemm(a, b, off))
