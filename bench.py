@@ -15,8 +15,14 @@ same metric through the public MoELayer call with pinned host buffers: each
 step copies hidden + logits host->device and the layer output device->host.
 The 22.5 GB of expert weights streamed every step exceed the 126 MB L2, so no
 flush is needed.  `--impl reference` times the CPU restatement of the
-reference's torch path (the oracle port) on the host cores.  With N > 1 each
-rank runs its own layer replica (weak scaling, no data-path collective).
+reference's torch path (the oracle port) on the host cores.
+
+With N > 1 (or --ep) the layer runs expert-parallel: each rank holds 4096
+tokens and E/N experts, tokens travel to their experts' ranks and back with
+NCCL all-to-alls (weak scaling in tokens; the experts are sharded).  The same
+line then carries "ep_combine": the BASELINE configs[3] dispatch + weighted
+combine (T=8192 tokens per rank, synthetic bf16 expert outputs) with its
+off-rank bytes and GB/s per GPU against the NVLink peer-copy figure.
 """
 from __future__ import annotations
 
@@ -362,6 +368,256 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# Expert-parallel arm (N > 1)
+# ---------------------------------------------------------------------------
+
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool's B200s
+EP_STAGES = ("gating", "ep_plan", "ep_dispatch_pack", "ep_dispatch_exchange",
+             "ep_expert_permute", "gate_up_swiglu_gemm", "down_gemm", "ep_combine_pack",
+             "ep_combine_exchange", "ep_combine_reduce")
+CFG3_TOKENS = 8192
+
+
+class Marker:
+    """mark(name) records a CUDA event on the current stream; ms() gives the
+    time between consecutive marks."""
+
+    def __init__(self):
+        import torch
+        self.torch = torch
+        self.events = []
+
+    def mark(self, name):
+        ev = self.torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.events.append((name, ev))
+
+    def ms(self) -> dict:
+        out = {}
+        for (_, a), (name, b) in zip(self.events, self.events[1:]):
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
+
+
+def route_launches(keys: int) -> int:
+    """Kernels of one route (moe_permute's counting sort): one CTA up to 4096
+    keys, else count + scan + rank."""
+    return 1 if keys <= 4096 else 3
+
+
+def run_ep(args):
+    import torch
+    import torch.distributed as dist
+
+    import layerstormexpertkernels_b200 as P
+    from layerstormexpertkernels_b200 import ep as EP
+    from layerstormexpertkernels_b200.synthetic import expert_weights, token_inputs
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def reduce(v: float, op) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    MAX = dist.ReduceOp.MAX if world > 1 else None
+    SUM = dist.ReduceOp.SUM if world > 1 else None
+    T, E = args.tokens, args.experts
+    El = E // world
+    w_gu, w_down = expert_weights(E, HIDDEN, INTER, device=dev,
+                                  experts=list(range(rank * El, (rank + 1) * El)))
+    x = token_inputs(T, E, HIDDEN, seed=rank)
+    bias = token_inputs(T, E, 8, seed=0).bias.to(dev)  # rank 0's bias, shared by all ranks
+    layer = EP.EPMoELayer(w_gu, w_down, bias, E, topk=TOPK, n_group=N_GROUP,
+                          topk_group=TOPK_GROUP, routed_scaling_factor=RSF, renormalize=True)
+    hidden, logits = x.hidden.to(dev), x.logits.to(dev)
+
+    for _ in range(args.warmup):
+        layer(hidden, logits)
+    torch.cuda.synchronize()
+    if P.device_error() != 0:
+        raise RuntimeError("a kernel reported a device-side error during warm-up")
+    w_r, idx_r = layer.gate(logits)
+    d = EP.dispatch(hidden, idx_r, w_r, E)
+    recv_rows, valid = d.recv_rows.shape[0], d.valid_slots
+    del d
+
+    markers = [Marker() for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    start.record()
+    for i in range(args.steps):
+        mk = markers[i]
+        mk.mark("start")
+        layer(hidden, logits, mark=mk.mark)
+    end.record()
+    torch.cuda.synchronize()
+    sampler.stop()
+    barrier()
+    ms = reduce(start.elapsed_time(end) / args.steps, MAX)
+    stage_ms = {s: statistics.mean(m.ms().get(s, 0.0) for m in markers) for s in EP_STAGES}
+    if P.device_error() != 0:
+        raise RuntimeError("a kernel reported a device-side error in the timed region")
+
+    # ---- end to end: pinned host tokens in, layer output out, every step
+    hidden_h, logits_h = x.hidden.pin_memory(), x.logits.pin_memory()
+    out_h = torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        hidden.copy_(hidden_h, non_blocking=True)
+        logits.copy_(logits_h, non_blocking=True)
+        out = layer(hidden, logits)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = reduce(e0.elapsed_time(e1) / args.steps, MAX)
+
+    ep_combine = ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier)
+
+    launches = (1 + (1 + route_launches(T * world) + 1) + 1 + (route_launches(recv_rows * TOPK) + 1)
+                + 2 + 2 + 1 + 1)
+    if rank == 0:
+        peaks = load_peaks()
+        gu_flops = 2.0 * valid * HIDDEN * 2 * INTER
+        gu_bytes = El * 2 * INTER * HIDDEN * 2 + valid * HIDDEN * 2 + valid * INTER * 2
+        gu_ms = stage_ms["gate_up_swiglu_gemm"]
+        achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
+        roofline = {"kernel": "gate_up_swiglu_gemm (rank 0)", "bound": "hbm",
+                    "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                    "traffic": None, "algorithmic_bytes": gu_bytes,
+                    "tensor_tflops": gu_flops / (gu_ms * 1e-3) / 1e12}
+        line = {"metric": METRIC, "value": world * T / (ms * 1e-3), "unit": UNIT,
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16",
+                "data": "synthetic (seeded randn tokens per rank; per-expert seeded N(0,0.02) bf16 weights)",
+                "config": {"workload": (f"cfg1 layer expert-parallel over {world} GPU(s): "
+                                        f"T={T} tokens per GPU, E={E} ({El} per GPU), H={HIDDEN}, "
+                                        f"I={INTER}, top-{TOPK}, NCCL all-to-all dispatch/combine"),
+                           "tokens_per_gpu": T, "global_tokens": world * T, "experts": E,
+                           "experts_per_gpu": El, "parallelism": f"ep{world}",
+                           "l2": "inputs larger than L2: expert weights and token rows per step"},
+                "gpu_launches": launches * args.steps,
+                "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": UNIT,
+                        "h2d_bytes_per_step": T * HIDDEN * 2 + T * E * 4,
+                        "d2h_bytes_per_step": T * HIDDEN * 2},
+                "roofline": roofline,
+                "stages_rank0_ms": stage_ms,
+                "ep_combine": ep_combine,
+                "clocks": sampler.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier):
+    """dispatch + weighted combine of T=8192 tokens per
+    rank with synthetic bf16 expert outputs (no GEMM); per-rank time is the
+    max over ranks."""
+    import torch
+
+    from layerstormexpertkernels_b200 import ep as EP
+    from layerstormexpertkernels_b200.synthetic import token_inputs
+
+    T = CFG3_TOKENS
+    El = E // world
+    x = token_inputs(T, E, HIDDEN, seed=100 + rank)
+    bias = token_inputs(T, E, 8, seed=100).bias.to(dev)
+    hidden, logits = x.hidden.to(dev), x.logits.to(dev)
+    import layerstormexpertkernels_b200 as P
+    w, idx = P.topk_gating(logits, bias, TOPK, N_GROUP, TOPK_GROUP, RSF, True)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    y_all = None
+
+    def step(mk=None):
+        nonlocal y_all
+        if mk:
+            mk.mark("start")
+        d = EP.dispatch(hidden, idx, w, E, mark=mk.mark if mk else None)
+        _, _, s2d = EP.expert_permute(d, El)
+        if y_all is None or y_all.shape[0] < d.valid_slots:
+            y_all = torch.randn(d.valid_slots, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+        if mk:
+            mk.mark("ep_expert_permute")
+        return EP.combine(d, y_all[:d.valid_slots], s2d, mark=mk.mark if mk else None)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(args.steps, 5)
+    marks = [Marker() for _ in range(steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        step(marks[i])
+    torch.cuda.synchronize()
+    barrier()
+    per = [m.ms() for m in marks]
+    disp = statistics.mean(p["ep_plan"] + p["ep_dispatch_pack"] + p["ep_dispatch_exchange"] +
+                           p["ep_expert_permute"] for p in per)
+    comb = statistics.mean(p["ep_combine_pack"] + p["ep_combine_exchange"] + p["ep_combine_reduce"]
+                           for p in per)
+    comb_x = statistics.mean(p["ep_combine_exchange"] for p in per)
+    disp_x = statistics.mean(p["ep_dispatch_exchange"] for p in per)
+    per_rank = El
+    own = torch.where((idx >= 0) & (idx < E), idx // per_rank, -1)
+    off_slots = int(((own != rank) & (own >= 0)).sum().item())
+    off_rows = 0
+    for gg in range(world):
+        if gg != rank:
+            off_rows += int((own == gg).any(dim=1).sum().item())
+    comb_bytes = off_slots * HIDDEN * 2
+    disp_bytes = off_rows * HIDDEN * 2
+    disp, comb = reduce(disp, MAX), reduce(comb, MAX)
+    comb_x, disp_x = reduce(comb_x, MAX), reduce(disp_x, MAX)
+    comb_bytes_all = reduce(float(comb_bytes), SUM)
+    disp_bytes_all = reduce(float(disp_bytes), SUM)
+    gbs = comb_bytes_all / world / (comb * 1e-3) / 1e9 if comb > 0 else 0.0
+    return {"workload": (f"cfg3: T={T} tokens per rank, E={E} over {world} rank(s), H={HIDDEN} "
+                         "bf16, top-8 sigmoid routing (8 groups / 4 kept), synthetic bf16 expert "
+                         "outputs, weighted per-slot combine with fp32 accumulation"),
+            "steps": steps,
+            "dispatch_ms": disp, "combine_ms": comb,
+            "dispatch_exchange_ms": disp_x, "combine_exchange_ms": comb_x,
+            "combine_offrank_bytes_per_gpu": comb_bytes_all / world,
+            "dispatch_offrank_bytes_per_gpu": disp_bytes_all / world,
+            "combine_gbs_per_gpu": gbs,
+            "combine_exchange_gbs_per_gpu": (comb_bytes_all / world / (comb_x * 1e-3) / 1e9
+                                             if comb_x > 0 else 0.0),
+            "dispatch_gbs_per_gpu": (disp_bytes_all / world / (disp * 1e-3) / 1e9
+                                     if disp > 0 else 0.0),
+            "nvlink_peak_gbs": NVLINK_GBS,
+            "nvlink_peak_source": "measured peer copy per direction per GPU on this pool",
+            "combine_frac_of_nvlink": gbs / NVLINK_GBS}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -372,11 +628,15 @@ def main():
     ap.add_argument("--experts", type=int, default=EXPERTS,
                     help="routed experts (default 256); smaller values make profiling cases")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep", action="store_true",
+                    help="run the expert-parallel arm even on one GPU (default for N > 1)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
+    elif args.ep or dist_env()[1] > 1:
+        run_ep(args)
     else:
         run_ours(args)
 

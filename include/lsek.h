@@ -248,6 +248,78 @@ LSEK_API lsek_status lsek_grouped_gemm_swiglu_bf16(void* Hout, const void* A,
                                           float swiglu_limit, void* workspace,
                                           size_t workspace_bytes, void* stream);
 
+/* ---- expert-parallel dispatch / combine ----------------------------------- */
+/* Experts are sharded over world_size ranks, rank g owning experts
+ * [g*E/G, (g+1)*E/G).  These kernels prepare and consume the two all-to-all
+ * exchanges (issued by the host over NCCL) of an expert-parallel layer; the
+ * result equals lsek_moe_unpermute_perslot followed by
+ * lsek_moe_combine_reduce_slots(bf16) on one GPU, bit for bit, for every
+ * world size.  The reference specifies this canonical per-slot combine
+ * (smxx/permute/moe_permute.h:67-99) and leaves the exchange to its consumer. */
+
+/* Scratch bytes for lsek_ep_plan. */
+LSEK_API size_t lsek_ep_plan_workspace_size(int32_t num_tokens, int32_t world_size);
+
+/* Send plan: send_off [G+1] (rank g's send rows are [send_off[g],
+ * send_off[g+1])), send_counts [G][2] (rows sent to rank g, and the
+ * (token, slot) pairs rank g serves), pair_row [T*G] (send row of token t
+ * for rank g; >= send_off[G] when t has no expert on g), row_pair [T*G]
+ * (inverse map).  Rows for a rank are in token order. */
+LSEK_API lsek_status lsek_ep_plan(int32_t* send_off, int32_t* send_counts, int32_t* pair_row,
+                         int32_t* row_pair, const int32_t* topk_indices,
+                         int32_t num_tokens, int32_t topk, int32_t num_experts,
+                         int32_t world_size, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* Fills the send rows [send_off[G], H] bf16 with each token's hidden row,
+ * and per row and slot the expert's index on the target rank (-1 when the
+ * slot's expert is on another rank) and the routing weight (0 there).  The
+ * buffers hold send_capacity rows (send_off[G]; rows past it are skipped). */
+LSEK_API lsek_status lsek_ep_dispatch_pack(void* send_rows, int32_t* send_ids, float* send_w,
+                                  int32_t send_capacity, const void* hidden, const int32_t* topk_indices,
+                                  const float* topk_weights, const int32_t* pair_row,
+                                  const int32_t* send_off, int32_t num_tokens,
+                                  int32_t topk, int32_t hidden_dim, int32_t num_experts,
+                                  int32_t world_size, void* stream);
+
+/* slot_row [rows+1]: exclusive scan of the number of ids >= 0 per row of
+ * ids [rows, topk]; slot_row[rows] = total. */
+LSEK_API lsek_status lsek_ep_slot_scan(int32_t* slot_row, const int32_t* ids, int32_t rows,
+                              int32_t topk, void* stream);
+
+/* Expert-side permute of the received rows by their local expert ids: as
+ * lsek_moe_permute with ids of -1 sorting last, except that rows of -1
+ * slots are not copied.  permuted holds permuted_rows rows (the number of
+ * valid slots; rows past it are never written). */
+LSEK_API lsek_status lsek_ep_expert_permute(void* permuted, int32_t permuted_rows,
+                                   int32_t* expert_offsets,
+                                   int32_t* src_to_dest_map, int32_t* permuted_idx,
+                                   const void* rows_in, const int32_t* local_ids,
+                                   int32_t rows, int32_t topk, int32_t hidden_dim,
+                                   int32_t local_experts, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* Combine rows, one per valid (received row i, slot j) in received-row and
+ * slot order, at slot_row[i] + (valid slots of i before j):
+ * bf16(w[i,j] * expert_out[src_to_dest_map[i*topk + j]]).  comb_rows holds
+ * comb_capacity rows (slot_row[rows]; rows past it are skipped). */
+LSEK_API lsek_status lsek_ep_combine_pack(void* comb_rows, int32_t comb_capacity,
+                                 const void* expert_out,
+                                 const int32_t* src_to_dest_map, const int32_t* ids,
+                                 const float* weights, const int32_t* slot_row,
+                                 int32_t rows, int32_t topk, int32_t hidden_dim,
+                                 void* stream);
+
+/* Sender side: out[t] = bf16(sum over slots j in order of the returned
+ * combine row of (t, j)), fp32 accumulation from 0; comb_rows holds the
+ * comb_count rows returned by all ranks in send-row order (never read past
+ * them), slot_row the scan of the sent ids. */
+LSEK_API lsek_status lsek_ep_combine_reduce(void* out, const void* comb_rows,
+                                   int32_t comb_count, const int32_t* topk_indices, const int32_t* pair_row,
+                                   const int32_t* slot_row, int32_t num_tokens,
+                                   int32_t topk, int32_t hidden_dim, int32_t num_experts,
+                                   int32_t world_size, void* stream);
+
 /* ---- whole MoE layer ------------------------------------------------------ */
 
 /* Scratch bytes for lsek_moe_layer_forward. */

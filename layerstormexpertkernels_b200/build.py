@@ -30,7 +30,7 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
 CU_SOURCES = ["common.cu", "gating.cu", "permute.cu", "swiglu.cu", "grouped_gemm.cu",
-              "layer.cu"]
+              "layer.cu", "ep.cu"]
 HEADERS = ["common.cuh", "swiglu.cuh"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = GENCODE + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",

@@ -370,6 +370,137 @@ void moe_layer_forward_out(torch::Tensor out, torch::Tensor hidden, torch::Tenso
       stream_of(hidden)));
 }
 
+// ---- expert-parallel device steps (the exchanges are issued from Python) --------
+
+void check_i32_cuda(const torch::Tensor& t, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.is_contiguous() && t.scalar_type() == at::kInt, what,
+              " must be a contiguous int32 CUDA tensor");
+}
+
+// Returns (send_off [G+1], send_counts [G, 2], pair_row [T*G], row_pair [T*G]).
+std::vector<torch::Tensor> ep_plan(torch::Tensor topk_indices, int64_t num_experts,
+                                   int64_t world_size) {
+  check_i32_cuda(topk_indices, "ep_plan: topk_indices");
+  TORCH_CHECK(topk_indices.dim() == 2, "ep_plan: topk_indices must be [T, topk]");
+  const c10::cuda::OptionalCUDAGuard guard(topk_indices.device());
+  const int64_t T = topk_indices.size(0), k = topk_indices.size(1);
+  auto opts = topk_indices.options();
+  auto send_off = torch::empty({world_size + 1}, opts);
+  auto send_counts = torch::empty({world_size, 2}, opts);
+  auto pair_row = torch::empty({T * world_size}, opts);
+  auto row_pair = torch::empty({T * world_size}, opts);
+  const size_t ws_bytes = lsek_ep_plan_workspace_size(to_i32(T, "T"), to_i32(world_size, "G"));
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes)}, opts.dtype(at::kByte));
+  check_status(lsek_ep_plan(send_off.data_ptr<int32_t>(), send_counts.data_ptr<int32_t>(),
+                            pair_row.data_ptr<int32_t>(),
+                            row_pair.data_ptr<int32_t>(), topk_indices.data_ptr<int32_t>(),
+                            to_i32(T, "T"), to_i32(k, "topk"), to_i32(num_experts, "E"),
+                            to_i32(world_size, "G"), ws.data_ptr(), ws_bytes,
+                            stream_of(topk_indices)));
+  return {send_off, send_counts, pair_row, row_pair};
+}
+
+// Returns (send_rows [rows, H], send_ids [rows, k], send_w [rows, k]).
+std::vector<torch::Tensor> ep_dispatch_pack(torch::Tensor hidden, torch::Tensor topk_indices,
+                                            torch::Tensor topk_weights, torch::Tensor pair_row,
+                                            torch::Tensor send_off, int64_t rows,
+                                            int64_t num_experts, int64_t world_size) {
+  TORCH_CHECK(hidden.is_cuda() && hidden.is_contiguous() && hidden.scalar_type() == at::kBFloat16,
+              "ep_dispatch_pack: hidden must be a contiguous bf16 CUDA tensor");
+  check_i32_cuda(topk_indices, "ep_dispatch_pack: topk_indices");
+  check_i32_cuda(pair_row, "ep_dispatch_pack: pair_row");
+  check_i32_cuda(send_off, "ep_dispatch_pack: send_off");
+  TORCH_CHECK(topk_weights.is_cuda() && topk_weights.is_contiguous() &&
+                  topk_weights.scalar_type() == at::kFloat,
+              "ep_dispatch_pack: topk_weights must be a contiguous float32 CUDA tensor");
+  const c10::cuda::OptionalCUDAGuard guard(hidden.device());
+  const int64_t T = hidden.size(0), H = hidden.size(1), k = topk_indices.size(1);
+  auto send_rows = torch::empty({rows, H}, hidden.options());
+  auto send_ids = torch::empty({rows, k}, topk_indices.options());
+  auto send_w = torch::empty({rows, k}, topk_weights.options());
+  check_status(lsek_ep_dispatch_pack(
+      send_rows.data_ptr(), send_ids.data_ptr<int32_t>(), send_w.data_ptr<float>(),
+      to_i32(rows, "rows"), hidden.data_ptr(),
+      topk_indices.data_ptr<int32_t>(), topk_weights.data_ptr<float>(), pair_row.data_ptr<int32_t>(),
+      send_off.data_ptr<int32_t>(), to_i32(T, "T"), to_i32(k, "topk"), to_i32(H, "H"),
+      to_i32(num_experts, "E"), to_i32(world_size, "G"), stream_of(hidden)));
+  return {send_rows, send_ids, send_w};
+}
+
+torch::Tensor ep_slot_scan(torch::Tensor ids) {
+  check_i32_cuda(ids, "ep_slot_scan: ids");
+  TORCH_CHECK(ids.dim() == 2, "ep_slot_scan: ids must be [rows, topk]");
+  const c10::cuda::OptionalCUDAGuard guard(ids.device());
+  auto out = torch::empty({ids.size(0) + 1}, ids.options());
+  check_status(lsek_ep_slot_scan(out.data_ptr<int32_t>(), ids.data_ptr<int32_t>(),
+                                 to_i32(ids.size(0), "rows"), to_i32(ids.size(1), "topk"),
+                                 stream_of(ids)));
+  return out;
+}
+
+// Returns (permuted [valid_slots, H], offsets [El+1], s2d [rows*k], perm [rows*k]).
+std::vector<torch::Tensor> ep_expert_permute(torch::Tensor rows_in, torch::Tensor local_ids,
+                                             int64_t local_experts, int64_t valid_slots) {
+  TORCH_CHECK(rows_in.is_cuda() && rows_in.is_contiguous() && rows_in.scalar_type() == at::kBFloat16,
+              "ep_expert_permute: rows must be a contiguous bf16 CUDA tensor");
+  check_i32_cuda(local_ids, "ep_expert_permute: local_ids");
+  const c10::cuda::OptionalCUDAGuard guard(rows_in.device());
+  const int64_t R = rows_in.size(0), H = rows_in.size(1), k = local_ids.size(1);
+  TORCH_CHECK(valid_slots >= 0 && valid_slots <= R * k, "ep_expert_permute: valid_slots out of range");
+  auto permuted = torch::empty({valid_slots, H}, rows_in.options());
+  auto offsets = torch::empty({local_experts + 1}, local_ids.options());
+  auto s2d = torch::empty({R * k}, local_ids.options());
+  auto perm = torch::empty({R * k}, local_ids.options());
+  const size_t ws_bytes = lsek_moe_permute_workspace_size(to_i32(R, "rows"), to_i32(k, "topk"),
+                                                          to_i32(local_experts, "E"));
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes)}, local_ids.options().dtype(at::kByte));
+  check_status(lsek_ep_expert_permute(
+      permuted.data_ptr(), to_i32(valid_slots, "valid_slots"), offsets.data_ptr<int32_t>(), s2d.data_ptr<int32_t>(),
+      perm.data_ptr<int32_t>(), rows_in.data_ptr(), local_ids.data_ptr<int32_t>(), to_i32(R, "rows"),
+      to_i32(k, "topk"), to_i32(H, "H"), to_i32(local_experts, "E"), ws.data_ptr(), ws_bytes,
+      stream_of(rows_in)));
+  return {permuted, offsets, s2d, perm};
+}
+
+torch::Tensor ep_combine_pack(torch::Tensor expert_out, torch::Tensor s2d, torch::Tensor ids,
+                              torch::Tensor weights, torch::Tensor slot_row, int64_t comb_rows) {
+  TORCH_CHECK(expert_out.is_cuda() && expert_out.is_contiguous() &&
+                  expert_out.scalar_type() == at::kBFloat16,
+              "ep_combine_pack: expert_out must be a contiguous bf16 CUDA tensor");
+  check_i32_cuda(s2d, "ep_combine_pack: s2d");
+  check_i32_cuda(ids, "ep_combine_pack: ids");
+  check_i32_cuda(slot_row, "ep_combine_pack: slot_row");
+  const c10::cuda::OptionalCUDAGuard guard(expert_out.device());
+  const int64_t H = expert_out.size(1);
+  auto comb = torch::empty({comb_rows, H}, expert_out.options());
+  check_status(lsek_ep_combine_pack(comb.data_ptr(), to_i32(comb_rows, "comb_rows"),
+                                    expert_out.data_ptr(), s2d.data_ptr<int32_t>(),
+                                    ids.data_ptr<int32_t>(), weights.data_ptr<float>(),
+                                    slot_row.data_ptr<int32_t>(), to_i32(ids.size(0), "rows"),
+                                    to_i32(ids.size(1), "topk"), to_i32(H, "H"),
+                                    stream_of(expert_out)));
+  return comb;
+}
+
+torch::Tensor ep_combine_reduce(torch::Tensor comb_rows, torch::Tensor topk_indices,
+                                torch::Tensor pair_row, torch::Tensor slot_row,
+                                int64_t num_experts, int64_t world_size) {
+  TORCH_CHECK(comb_rows.is_cuda() && comb_rows.is_contiguous() &&
+                  comb_rows.scalar_type() == at::kBFloat16,
+              "ep_combine_reduce: comb_rows must be a contiguous bf16 CUDA tensor");
+  check_i32_cuda(topk_indices, "ep_combine_reduce: topk_indices");
+  const c10::cuda::OptionalCUDAGuard guard(comb_rows.device());
+  const int64_t T = topk_indices.size(0), k = topk_indices.size(1), H = comb_rows.size(1);
+  auto out = torch::empty({T, H}, comb_rows.options());
+  check_status(lsek_ep_combine_reduce(out.data_ptr(), comb_rows.data_ptr(),
+                                      to_i32(comb_rows.size(0), "comb_rows"),
+                                      topk_indices.data_ptr<int32_t>(), pair_row.data_ptr<int32_t>(),
+                                      slot_row.data_ptr<int32_t>(), to_i32(T, "T"), to_i32(k, "topk"),
+                                      to_i32(H, "H"), to_i32(num_experts, "E"),
+                                      to_i32(world_size, "G"), stream_of(comb_rows)));
+  return out;
+}
+
 // Timing events for lsek_moe_layer_forward's stage_events: created with
 // timing enabled, recorded by the library on the layer's stream, read back
 // as milliseconds between consecutive events.
@@ -455,6 +586,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("renormalize"), py::arg("scoring_func"), py::arg("swiglu_limit"),
         py::arg("workspace"), py::arg("topk_weights") = py::none(),
         py::arg("topk_indices") = py::none(), py::arg("stage_events") = std::vector<int64_t>{});
+  m.def("ep_plan", &ep_plan, py::arg("topk_indices"), py::arg("num_experts"),
+        py::arg("world_size"));
+  m.def("ep_dispatch_pack", &ep_dispatch_pack, py::arg("hidden"), py::arg("topk_indices"),
+        py::arg("topk_weights"), py::arg("pair_row"), py::arg("send_off"), py::arg("rows"),
+        py::arg("num_experts"), py::arg("world_size"));
+  m.def("ep_slot_scan", &ep_slot_scan, py::arg("ids"));
+  m.def("ep_expert_permute", &ep_expert_permute, py::arg("rows"), py::arg("local_ids"),
+        py::arg("local_experts"), py::arg("valid_slots"));
+  m.def("ep_combine_pack", &ep_combine_pack, py::arg("expert_out"), py::arg("s2d"), py::arg("ids"),
+        py::arg("weights"), py::arg("slot_row"), py::arg("comb_rows"));
+  m.def("ep_combine_reduce", &ep_combine_reduce, py::arg("comb_rows"), py::arg("topk_indices"),
+        py::arg("pair_row"), py::arg("slot_row"), py::arg("num_experts"), py::arg("world_size"));
   m.def("events_create", &events_create, py::arg("n"));
   m.def("events_elapsed_ms", &events_elapsed_ms, py::arg("handles"));
   m.def("events_destroy", &events_destroy, py::arg("handles"));

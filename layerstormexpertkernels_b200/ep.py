@@ -1,0 +1,239 @@
+"""Expert-parallel MoE layer: experts sharded over the ranks of a process
+group, tokens exchanged with two NCCL all-to-alls.
+
+Rank g of G owns experts [g*E/G, (g+1)*E/G).  Per layer:
+
+  1. gate locally (topk_gating on this rank's tokens);
+  2. plan: a stable counting sort of (token, destination rank) pairs gives
+     each destination's send rows in token order, and per destination the
+     number of rows and of (token, slot) pairs it serves; the [G, 2] counts
+     go through one small all-to-all and one device->host copy (the only
+     host synchronisation of the layer);
+  3. dispatch: each token row once per distinct owner rank, with per slot
+     the expert's local index (-1 for other ranks' experts) and weight;
+  4. expert side: permute the received rows by local expert (only own
+     slots are copied), gate/up GEMM with fused SwiGLU, down GEMM, then the
+     weighted per-slot pack bf16(w * y) in received-row and slot order;
+  5. combine: the packed slots go back with the reverse all-to-all;
+  6. the source rank sums each token's slots in slot order in fp32 from 0
+     and rounds once to bf16.
+
+Steps 4-6 reproduce moe_unpermute_bf16_perslot followed by
+moe_combine_reduce_slots_bf16_to_bf16 (smxx/permute/moe_permute.h:67-99 of
+the reference) bit for bit, for every world size: the per-slot product and
+the fixed-order sum are the same operations on the same values.  The
+reference leaves the exchange to its consumer and models it as an
+all-reduce of [T, topk, H] (tests/test_kernels.py:131-142, 187-200); only
+the rows that cross ranks travel here.
+
+Every data-path step is a CUDA kernel of liblsek.so (`DeviceSteps`); the
+collectives are torch.distributed all_to_all_single calls
+(`ProcessGroupExchange`).  Both can be replaced: the CPU tests inject a
+restatement of the kernels to check this module's exchange logic over gloo,
+and the one-GPU tests run G ranks as threads with an in-process exchange.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _C
+
+
+class DeviceSteps:
+    """The device kernels of each EP step (liblsek.so through the binding)."""
+
+    plan = staticmethod(_C.ep_plan)
+    dispatch_pack = staticmethod(_C.ep_dispatch_pack)
+    slot_scan = staticmethod(_C.ep_slot_scan)
+    expert_permute = staticmethod(_C.ep_expert_permute)
+    combine_pack = staticmethod(_C.ep_combine_pack)
+    combine_reduce = staticmethod(_C.ep_combine_reduce)
+    topk_gating = staticmethod(_C.topk_gating)
+    grouped_gemm_swiglu = staticmethod(_C.grouped_gemm_swiglu_bf16)
+    grouped_gemm = staticmethod(_C.grouped_gemm_bf16)
+
+
+def _as_words(t: torch.Tensor) -> torch.Tensor:
+    """A 2-D tensor viewed as 32-bit words (bf16 rows travel as int32 pairs,
+    which every backend moves bit for bit)."""
+    if t.dtype in (torch.int32, torch.float32):
+        return t
+    return t.view(torch.int32)
+
+
+class ProcessGroupExchange:
+    """The exchange over a torch.distributed process group (NCCL on GPUs,
+    gloo on CPU); with no initialised group it is a single rank."""
+
+    def __init__(self, group=None):
+        self.group = group
+        if dist.is_available() and dist.is_initialized():
+            self.world_size, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        else:
+            self.world_size, self.rank = 1, 0
+
+    def all_to_all(self, send: torch.Tensor, send_splits: list[int],
+                   recv_splits: list[int]) -> torch.Tensor:
+        """Variable all-to-all along dim 0; identity when there is one rank."""
+        if self.world_size == 1:
+            return send
+        recv = send.new_empty((sum(recv_splits),) + tuple(send.shape[1:]))
+        dist.all_to_all_single(_as_words(recv), _as_words(send), output_split_sizes=recv_splits,
+                               input_split_sizes=send_splits, group=self.group)
+        return recv
+
+
+def as_exchange(group):
+    """`group` may be None (the default process group, or one rank without
+    one), a torch.distributed process group, or any object with world_size,
+    rank and all_to_all(send, send_splits, recv_splits)."""
+    if hasattr(group, "all_to_all"):
+        return group
+    return ProcessGroupExchange(group)
+
+
+@dataclass
+class Dispatch:
+    """State of one dispatch, needed again by the combine.
+
+    Sender side: the token routing, the plan and the sent slot ids.
+    Expert side: the received rows, local ids and weights, and the split
+    sizes of both exchanges (host ints)."""
+
+    num_tokens: int
+    num_experts: int
+    world_size: int
+    topk_indices: torch.Tensor          # [T, k] this rank's routing
+    pair_row: torch.Tensor              # [T*G] send row of (token, rank)
+    send_ids: torch.Tensor              # [rows, k] local ids at the destination
+    send_rows_n: list[int]              # rows sent to each rank
+    send_slots_n: list[int]             # (token, slot) pairs served by each rank
+    recv_rows: torch.Tensor             # [R, H] bf16
+    recv_ids: torch.Tensor              # [R, k] int32, -1 = another rank's expert
+    recv_w: torch.Tensor                # [R, k] fp32, 0 there
+    recv_rows_n: list[int]
+    recv_slots_n: list[int]
+
+    @property
+    def valid_slots(self) -> int:
+        return sum(self.recv_slots_n)
+
+
+def dispatch(hidden: torch.Tensor, topk_indices: torch.Tensor, topk_weights: torch.Tensor,
+             num_experts: int, group=None, steps=DeviceSteps,
+             mark: Optional[Callable[[str], None]] = None) -> Dispatch:
+    """Sends each token row to every rank that owns one of its experts.
+    `mark(name)` (optional) is called after each phase, e.g. to record
+    timing events."""
+    ex = as_exchange(group)
+    world = ex.world_size
+    T, k = topk_indices.shape
+    send_off, send_counts, pair_row, _ = steps.plan(topk_indices, num_experts, world)
+    recv_counts = ex.all_to_all(send_counts, [1] * world, [1] * world)
+    counts = torch.cat([send_counts.reshape(-1), recv_counts.reshape(-1)]).cpu().tolist()
+    send_rows_n, send_slots_n = counts[0:2 * world:2], counts[1:2 * world:2]
+    recv_rows_n, recv_slots_n = counts[2 * world::2], counts[2 * world + 1::2]
+    if mark:
+        mark("ep_plan")
+    send_rows, send_ids, send_w = steps.dispatch_pack(hidden, topk_indices, topk_weights, pair_row,
+                                                      send_off, sum(send_rows_n), num_experts,
+                                                      world)
+    if mark:
+        mark("ep_dispatch_pack")
+    recv_rows = ex.all_to_all(send_rows, send_rows_n, recv_rows_n)
+    recv_ids = ex.all_to_all(send_ids, send_rows_n, recv_rows_n)
+    recv_w = ex.all_to_all(send_w, send_rows_n, recv_rows_n)
+    if mark:
+        mark("ep_dispatch_exchange")
+    return Dispatch(T, num_experts, world, topk_indices, pair_row, send_ids, send_rows_n,
+                    send_slots_n, recv_rows, recv_ids, recv_w, recv_rows_n, recv_slots_n)
+
+
+def combine(d: Dispatch, expert_out: torch.Tensor, src_to_dest_map: torch.Tensor, group=None,
+            steps=DeviceSteps, mark: Optional[Callable[[str], None]] = None) -> torch.Tensor:
+    """Weighted combine of the expert outputs back onto the source tokens.
+
+    `expert_out` [valid_slots, H] bf16 holds the expert-side rows in the
+    order of `src_to_dest_map` (the map returned by expert_permute)."""
+    slot_row = steps.slot_scan(d.recv_ids)
+    comb = steps.combine_pack(expert_out, src_to_dest_map, d.recv_ids, d.recv_w, slot_row,
+                              d.valid_slots)
+    if mark:
+        mark("ep_combine_pack")
+    back = as_exchange(group).all_to_all(comb, d.recv_slots_n, d.send_slots_n)
+    if mark:
+        mark("ep_combine_exchange")
+    send_slot_row = steps.slot_scan(d.send_ids)
+    out = steps.combine_reduce(back, d.topk_indices, d.pair_row, send_slot_row, d.num_experts,
+                               d.world_size)
+    if mark:
+        mark("ep_combine_reduce")
+    return out
+
+
+def expert_permute(d: Dispatch, local_experts: int, steps=DeviceSteps):
+    """Expert-major order of this rank's received slots:
+    (permuted [valid_slots, H], offsets [local_experts+1], src_to_dest_map)."""
+    permuted, offsets, s2d, _ = steps.expert_permute(d.recv_rows, d.recv_ids, local_experts,
+                                                     d.valid_slots)
+    return permuted, offsets, s2d
+
+
+class EPMoELayer:
+    """The routed-expert MoE layer with this rank's share of the experts.
+
+    `w_gu` [E/G, 2I, H] and `w_down` [E/G, H, I] are the local experts'
+    weights (gate rows first, as grouped_gemm_swiglu_bf16 expects); `bias` is
+    the full [E] correction bias.  forward(hidden [T, H] bf16, logits [T, E]
+    fp32) returns this rank's [T, H] bf16 layer output."""
+
+    def __init__(self, w_gu: torch.Tensor, w_down: torch.Tensor, bias: Optional[torch.Tensor],
+                 num_experts: int, topk: int = 8, n_group: int = 8, topk_group: int = 4,
+                 routed_scaling_factor: float = 2.5, renormalize: bool = True,
+                 scoring_func: str = "sigmoid", swiglu_limit: float = 0.0, group=None,
+                 steps=DeviceSteps):
+        group = as_exchange(group)
+        world = group.world_size
+        if num_experts % world:
+            raise ValueError(f"num_experts={num_experts} is not a multiple of world size {world}")
+        if w_gu.shape[0] != num_experts // world or w_down.shape[0] != num_experts // world:
+            raise ValueError("w_gu / w_down must hold num_experts / world_size local experts")
+        self.w_gu, self.w_down, self.bias = w_gu, w_down, bias
+        self.num_experts, self.local_experts = num_experts, num_experts // world
+        self.topk, self.n_group, self.topk_group = topk, n_group, topk_group
+        self.routed_scaling_factor, self.renormalize = routed_scaling_factor, renormalize
+        self.scoring_func, self.swiglu_limit = scoring_func, swiglu_limit
+        self.group, self.steps = group, steps
+
+    def gate(self, logits: torch.Tensor):
+        return self.steps.topk_gating(logits, self.bias, self.topk, self.n_group, self.topk_group,
+                                      self.routed_scaling_factor, self.renormalize,
+                                      self.scoring_func)
+
+    def experts(self, d: Dispatch, mark=None):
+        """Expert side: permute, gate/up + SwiGLU, down.  Returns (y, s2d)."""
+        permuted, offsets, s2d = expert_permute(d, self.local_experts, self.steps)
+        if mark:
+            mark("ep_expert_permute")
+        h = self.steps.grouped_gemm_swiglu(permuted, self.w_gu, offsets, self.swiglu_limit)
+        if mark:
+            mark("gate_up_swiglu_gemm")
+        y = self.steps.grouped_gemm(h, self.w_down, offsets)
+        if mark:
+            mark("down_gemm")
+        return y, s2d
+
+    def forward(self, hidden: torch.Tensor, logits: torch.Tensor,
+                mark: Optional[Callable[[str], None]] = None) -> torch.Tensor:
+        w, idx = self.gate(logits)
+        if mark:
+            mark("gating")
+        d = dispatch(hidden, idx, w, self.num_experts, self.group, self.steps, mark)
+        y, s2d = self.experts(d, mark)
+        return combine(d, y, s2d, self.group, self.steps, mark)
+
+    __call__ = forward

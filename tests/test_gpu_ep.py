@@ -1,0 +1,199 @@
+"""GPU parity of the expert-parallel dispatch/combine kernels.
+
+1. Each EP kernel against its CPU restatement (oracle/ep_oracle.py), bit
+   for bit, for world sizes 1-8 and sizes on both sides of the one-CTA route.
+2. The whole EP layer (layerstormexpertkernels_b200.ep) with G ranks run as
+   threads on one GPU, against the one-GPU canonical path made of the
+   reference-surface ops (topk_gating, moe_permute, the grouped GEMMs,
+   moe_unpermute_bf16_perslot, moe_combine_reduce_slots_bf16_to_bf16):
+   identical bits for every G.
+3. The same over NCCL with 2 processes when the box has 2 GPUs."""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import bits, bf16_dev, dev, f32, sync_and_check_device_error
+from oracle import ep_oracle as EO
+from oracle import moe_oracle as MO
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _routing(T, E, k, seed, invalid=True):
+    rng = np.random.default_rng(seed)
+    idx = np.array([rng.choice(E, k, replace=False) for _ in range(T)],
+                   dtype=np.int32).reshape(T, k)
+    if invalid and T > 2:
+        idx[1, 0] = -1
+        idx[T - 1, k - 1] = E + 5
+    w = rng.random((T, k), dtype=np.float32)
+    return idx, w
+
+
+@pytest.mark.parametrize("G", [1, 2, 4, 8])
+@pytest.mark.parametrize("T", [0, 1, 37, 700, 5000])
+def test_plan_matches_oracle(G, T):
+    import layerstormexpertkernels_b200 as P
+    E, k = 64, 8
+    idx, _ = _routing(T, E, k, seed=T * 10 + G)
+    off, counts, pair_row, row_pair = P._C.ep_plan(dev(idx), E, G)
+    sync_and_check_device_error()
+    o_off, o_counts, o_pr, o_rp = EO.ep_plan(idx, E, G)
+    assert off.cpu().numpy().tolist() == o_off.tolist()
+    assert counts.cpu().numpy().tolist() == o_counts.tolist()
+    if T:
+        assert np.array_equal(pair_row.cpu().numpy(), o_pr)
+        assert np.array_equal(row_pair.cpu().numpy(), o_rp)
+
+
+@pytest.mark.parametrize("G", [1, 2, 8])
+@pytest.mark.parametrize("T,H", [(1, 64), (37, 7168), (700, 256)])
+def test_dispatch_pack_and_slot_scan(G, T, H):
+    import layerstormexpertkernels_b200 as P
+    E, k = 64, 8
+    idx, w = _routing(T, E, k, seed=T + G)
+    hidden = MO.bf16_round(np.random.default_rng(T).standard_normal((T, H), dtype=np.float32))
+    off, counts, pair_row, _ = P._C.ep_plan(dev(idx), E, G)
+    rows = int(off[G].item())
+    sr, sid, sw = P._C.ep_dispatch_pack(bf16_dev(hidden), dev(idx), dev(w), pair_row, off, rows,
+                                        E, G)
+    scan = P._C.ep_slot_scan(sid)
+    sync_and_check_device_error()
+    o_sr, o_sid, o_sw = EO.ep_dispatch_pack(hidden, idx, w, pair_row.cpu().numpy(),
+                                            off.cpu().numpy(), E, G)
+    assert np.array_equal(bits(sr), MO.bf16_bits(o_sr))
+    assert np.array_equal(sid.cpu().numpy(), o_sid)
+    assert np.array_equal(sw.cpu().numpy().view(np.uint32), o_sw.view(np.uint32))
+    assert np.array_equal(scan.cpu().numpy(), EO.ep_slot_scan(o_sid))
+    assert int(scan[-1].item()) == int(counts[:, 1].sum().item())
+
+
+@pytest.mark.parametrize("R,El,k,H", [(1, 4, 8, 64), (300, 32, 8, 256), (1500, 32, 8, 128),
+                                      (200, 1, 4, 7168)])
+def test_expert_permute_and_combine(R, El, k, H):
+    """Expert side: permute with -1 sentinels (multi-CTA route above 4096
+    slots), then the weighted per-slot pack; sender side: the reduce."""
+    import layerstormexpertkernels_b200 as P
+    rng = np.random.default_rng(R + El)
+    ids = rng.integers(-1, El, size=(R, k)).astype(np.int32)
+    w = np.where(ids >= 0, rng.random((R, k), dtype=np.float32), 0).astype(np.float32)
+    rows = MO.bf16_round(rng.standard_normal((R, H), dtype=np.float32))
+    nv = int((ids >= 0).sum())
+    permuted, offs, s2d, perm = P._C.ep_expert_permute(bf16_dev(rows), dev(ids), El, nv)
+    sync_and_check_device_error()
+    o_p, o_off, o_s2d, o_perm = EO.ep_expert_permute(rows, ids, El)
+    assert offs.cpu().numpy().tolist() == o_off.tolist()
+    assert np.array_equal(s2d.cpu().numpy(), o_s2d)
+    assert np.array_equal(perm.cpu().numpy(), o_perm)
+    assert np.array_equal(bits(permuted), MO.bf16_bits(o_p))
+    # a synthetic expert output per permuted row
+    y = MO.bf16_round(rng.standard_normal((nv, H), dtype=np.float32))
+    slot_row = P._C.ep_slot_scan(dev(ids))
+    comb = P._C.ep_combine_pack(bf16_dev(y), s2d, dev(ids), dev(w), slot_row, nv)
+    sync_and_check_device_error()
+    o_comb = EO.ep_combine_pack(y, o_s2d, ids, w, slot_row.cpu().numpy())
+    assert np.array_equal(bits(comb), MO.bf16_bits(o_comb))
+
+
+@pytest.mark.parametrize("G", [1, 2, 4, 8])
+@pytest.mark.parametrize("T,H", [(1, 64), (100, 7168), (900, 256)])
+def test_combine_reduce_matches_oracle(G, T, H):
+    import layerstormexpertkernels_b200 as P
+    E, k = 64, 8
+    idx, _ = _routing(T, E, k, seed=7 * T + G)
+    off, counts, pair_row, _ = EO.ep_plan(idx, E, G)
+    send_ids = EO.ep_dispatch_pack(np.zeros((T, 8), np.float32), idx, np.ones((T, k), np.float32),
+                                   pair_row, off, E, G)[1]
+    slot_row = EO.ep_slot_scan(send_ids)
+    comb = MO.bf16_round(np.random.default_rng(T).standard_normal((int(slot_row[-1]), H),
+                                                                   dtype=np.float32))
+    out = P._C.ep_combine_reduce(bf16_dev(comb), dev(idx), dev(pair_row), dev(slot_row), E, G)
+    sync_and_check_device_error()
+    ref = EO.ep_combine_reduce(comb, idx, pair_row, slot_row, E, G)
+    assert np.array_equal(bits(out), MO.bf16_bits(ref))
+
+
+# ---------------------------------------------------------------------------
+# the whole EP layer: G ranks as threads on one GPU
+# ---------------------------------------------------------------------------
+
+E_L, H_L, I_L, K_L = 64, 512, 256, 8
+
+
+def _layer_setup(G, tokens):
+    from layerstormexpertkernels_b200.synthetic import expert_weights, token_inputs
+    w_gu, w_down = expert_weights(E_L, H_L, I_L, device="cuda", seed_base=7000)
+    toks = [token_inputs(tokens[r], E_L, H_L, seed=100 + r) for r in range(G)]
+    return w_gu, w_down, toks
+
+
+def canonical_gpu(x, w_gu, w_down, bias):
+    """The one-GPU canonical path through the reference-surface ops."""
+    import layerstormexpertkernels_b200 as P
+    hidden, logits = x.hidden.cuda(), x.logits.cuda()
+    w, idx = P.topk_gating(logits, bias, K_L, 8, 4, 2.5, True)
+    permuted, offs, s2d, _ = P.moe_permute(hidden, idx, E_L)
+    h = P.grouped_gemm_swiglu_bf16(permuted, w_gu, offs)
+    y = P.grouped_gemm_bf16(h, w_down, offs)
+    perslot = P.moe_unpermute_bf16_perslot(y, w, s2d, hidden.shape[0], K_L)
+    return P.moe_combine_reduce_slots_bf16_to_bf16(perslot)
+
+
+@pytest.mark.parametrize("G,tokens", [(1, [300]), (2, [300, 257]), (4, [64, 1, 200, 90]),
+                                      (8, [130] * 8)])
+def test_ep_layer_threads_bit_exact(G, tokens):
+    from ep_loopback import LoopbackHub
+    from layerstormexpertkernels_b200.ep import EPMoELayer
+
+    w_gu, w_down, toks = _layer_setup(G, tokens)
+    bias = toks[0].bias.cuda()
+    El = E_L // G
+    stages = [[] for _ in range(G)]
+
+    def rank_fn(r, ex):
+        layer = EPMoELayer(w_gu[r * El:(r + 1) * El].contiguous(),
+                           w_down[r * El:(r + 1) * El].contiguous(), bias, E_L, topk=K_L,
+                           group=ex)
+        return layer(toks[r].hidden.cuda(), toks[r].logits.cuda(), mark=stages[r].append)
+
+    outs = LoopbackHub(G).run(rank_fn)
+    sync_and_check_device_error()
+    for r in range(G):
+        ref = canonical_gpu(toks[r], w_gu, w_down, bias)
+        assert torch.equal(outs[r].view(torch.int16), ref.view(torch.int16)), f"rank {r}"
+        assert stages[r][0] == "gating" and stages[r][-1] == "ep_combine_reduce"
+
+
+def test_ep_layer_one_rank_process_group_free():
+    """No process group: ProcessGroupExchange is a single rank."""
+    from layerstormexpertkernels_b200.ep import EPMoELayer
+    w_gu, w_down, toks = _layer_setup(1, [150])
+    bias = toks[0].bias.cuda()
+    out = EPMoELayer(w_gu, w_down, bias, E_L, topk=K_L)(toks[0].hidden.cuda(),
+                                                        toks[0].logits.cuda())
+    ref = canonical_gpu(toks[0], w_gu, w_down, bias)
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+def test_ep_layer_nccl_two_gpus(tmp_path):
+    """Two processes over NCCL (one GPU each), each checking its tokens
+    against the one-GPU canonical path on its own GPU."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", "29641",
+           os.path.join(ROOT, "tests", "ep_nccl_worker.py"), str(tmp_path)]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    res = subprocess.run(["timeout", "-k", "30", "600"] + cmd, cwd=ROOT, env=env,
+                         capture_output=True, text=True)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    for r in range(2):
+        assert (tmp_path / f"ok{r}").read_text() == "bit-exact"
