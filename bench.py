@@ -373,9 +373,6 @@ def run_ours(args):
 # ---------------------------------------------------------------------------
 
 NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool's B200s
-EP_STAGES = ("gating", "ep_plan", "ep_dispatch_pack", "ep_dispatch_exchange",
-             "ep_expert_permute", "gate_up_swiglu_gemm", "down_gemm", "ep_combine_pack",
-             "ep_combine_exchange", "ep_combine_reduce")
 CFG3_TOKENS = 8192
 
 
@@ -398,6 +395,11 @@ class Marker:
         for (_, a), (name, b) in zip(self.events, self.events[1:]):
             out[name] = out.get(name, 0.0) + a.elapsed_time(b)
         return out
+
+
+def mean_stages(markers) -> dict:
+    per = [m.ms() for m in markers]
+    return {name: statistics.mean(p.get(name, 0.0) for p in per) for name in per[0]}
 
 
 def route_launches(keys: int) -> int:
@@ -440,8 +442,11 @@ def run_ep(args):
                                   experts=list(range(rank * El, (rank + 1) * El)))
     x = token_inputs(T, E, HIDDEN, seed=rank)
     bias = token_inputs(T, E, 8, seed=0).bias.to(dev)  # rank 0's bias, shared by all ranks
+    peer = args.transport == "peer"
+    domain = EP.PeerDomain(max(T, CFG3_TOKENS), HIDDEN, TOPK) if peer else None
     layer = EP.EPMoELayer(w_gu, w_down, bias, E, topk=TOPK, n_group=N_GROUP,
-                          topk_group=TOPK_GROUP, routed_scaling_factor=RSF, renormalize=True)
+                          topk_group=TOPK_GROUP, routed_scaling_factor=RSF, renormalize=True,
+                          domain=domain)
     hidden, logits = x.hidden.to(dev), x.logits.to(dev)
 
     for _ in range(args.warmup):
@@ -450,8 +455,15 @@ def run_ep(args):
     if P.device_error() != 0:
         raise RuntimeError("a kernel reported a device-side error during warm-up")
     w_r, idx_r = layer.gate(logits)
-    d = EP.dispatch(hidden, idx_r, w_r, E)
-    recv_rows, valid = d.recv_rows.shape[0], d.valid_slots
+    if peer:
+        d = EP.peer_dispatch(domain, hidden, idx_r, w_r, E)
+        recv_rows, valid = d.recv_rows.shape[0], d.valid_slots
+        # finish the epoch so every rank's flags stay in step
+        _, _, s2d0, _ = P._C.ep_expert_permute(d.recv_rows, d.recv_ids, El, valid)
+        EP.peer_combine(d, torch.zeros(valid, HIDDEN, dtype=torch.bfloat16, device=dev), s2d0)
+    else:
+        d = EP.dispatch(hidden, idx_r, w_r, E)
+        recv_rows, valid = d.recv_rows.shape[0], d.valid_slots
     del d
 
     markers = [Marker() for _ in range(args.steps)]
@@ -471,7 +483,7 @@ def run_ep(args):
     sampler.stop()
     barrier()
     ms = reduce(start.elapsed_time(end) / args.steps, MAX)
-    stage_ms = {s: statistics.mean(m.ms().get(s, 0.0) for m in markers) for s in EP_STAGES}
+    stage_ms = mean_stages(markers)
     if P.device_error() != 0:
         raise RuntimeError("a kernel reported a device-side error in the timed region")
 
@@ -498,15 +510,22 @@ def run_ep(args):
     barrier()
     e2e_ms = reduce(e0.elapsed_time(e1) / args.steps, MAX)
 
-    ep_combine = ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier)
+    ep_combine = ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier, domain)
 
-    launches = (1 + (1 + route_launches(T * world) + 1) + 1 + (route_launches(recv_rows * TOPK) + 1)
-                + 2 + 2 + 1 + 1)
+    plan = 1 + route_launches(T * world) + 1
+    permute = route_launches(recv_rows * TOPK) + 1
+    if peer:  # gating, plan, push, wait, permute, gate/up, scan, combine plan, down+combine, wait, scan, reduce
+        launches = 1 + plan + 1 + 1 + permute + 1 + 1 + 1 + 1 + 1 + 1 + 1
+    else:     # gating, plan, pack, permute, gate/up, down, scan, combine pack, scan, reduce
+        launches = 1 + plan + 1 + permute + 2 + 2 + 1 + 1
     if rank == 0:
         peaks = load_peaks()
         gu_flops = 2.0 * valid * HIDDEN * 2 * INTER
         gu_bytes = El * 2 * INTER * HIDDEN * 2 + valid * HIDDEN * 2 + valid * INTER * 2
         gu_ms = stage_ms["gate_up_swiglu_gemm"]
+        transport = ("peer memory: dispatch kernel stores rows into the owner GPUs, combine "
+                     "fused into the down-GEMM epilogue (NVLink stores), epoch flags"
+                     if peer else "NCCL all-to-all dispatch/combine")
         achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
         roofline = {"kernel": "gate_up_swiglu_gemm (rank 0)", "bound": "hbm",
                     "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -520,7 +539,8 @@ def run_ep(args):
                 "data": "synthetic (seeded randn tokens per rank; per-expert seeded N(0,0.02) bf16 weights)",
                 "config": {"workload": (f"cfg1 layer expert-parallel over {world} GPU(s): "
                                         f"T={T} tokens per GPU, E={E} ({El} per GPU), H={HIDDEN}, "
-                                        f"I={INTER}, top-{TOPK}, NCCL all-to-all dispatch/combine"),
+                                        f"I={INTER}, top-{TOPK}"),
+                           "transport": transport,
                            "tokens_per_gpu": T, "global_tokens": world * T, "experts": E,
                            "experts_per_gpu": El, "parallelism": f"ep{world}",
                            "l2": "inputs larger than L2: expert weights and token rows per step"},
@@ -533,11 +553,13 @@ def run_ep(args):
                 "ep_combine": ep_combine,
                 "clocks": sampler.summary()}
         print(json.dumps(line), flush=True)
+    if domain is not None:
+        domain.close()
     if world > 1:
         dist.destroy_process_group()
 
 
-def ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier):
+def ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier, domain=None):
     """dispatch + weighted combine of T=8192 tokens per
     rank with synthetic bf16 expert outputs (no GEMM); per-rank time is the
     max over ranks."""
@@ -558,15 +580,22 @@ def ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier):
 
     def step(mk=None):
         nonlocal y_all
+        mark = mk.mark if mk else None
         if mk:
             mk.mark("start")
-        d = EP.dispatch(hidden, idx, w, E, mark=mk.mark if mk else None)
-        _, _, s2d = EP.expert_permute(d, El)
+        if domain is not None:
+            d = EP.peer_dispatch(domain, hidden, idx, w, E, mark=mark)
+            _, _, s2d, _ = P._C.ep_expert_permute(d.recv_rows, d.recv_ids, El, d.valid_slots)
+        else:
+            d = EP.dispatch(hidden, idx, w, E, mark=mark)
+            _, _, s2d = EP.expert_permute(d, El)
         if y_all is None or y_all.shape[0] < d.valid_slots:
             y_all = torch.randn(d.valid_slots, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
         if mk:
             mk.mark("ep_expert_permute")
-        return EP.combine(d, y_all[:d.valid_slots], s2d, mark=mk.mark if mk else None)
+        if domain is not None:
+            return EP.peer_combine(d, y_all[:d.valid_slots], s2d, mark=mark)
+        return EP.combine(d, y_all[:d.valid_slots], s2d, mark=mark)
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -579,13 +608,19 @@ def ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier):
         step(marks[i])
     torch.cuda.synchronize()
     barrier()
-    per = [m.ms() for m in marks]
-    disp = statistics.mean(p["ep_plan"] + p["ep_dispatch_pack"] + p["ep_dispatch_exchange"] +
-                           p["ep_expert_permute"] for p in per)
-    comb = statistics.mean(p["ep_combine_pack"] + p["ep_combine_exchange"] + p["ep_combine_reduce"]
-                           for p in per)
-    comb_x = statistics.mean(p["ep_combine_exchange"] for p in per)
-    disp_x = statistics.mean(p["ep_dispatch_exchange"] for p in per)
+    st = mean_stages(marks)
+    if domain is not None:
+        disp_names = ("ep_plan", "ep_dispatch_push", "ep_dispatch_wait", "ep_expert_permute")
+        comb_names = ("ep_combine_push", "ep_combine_wait", "ep_combine_reduce")
+        disp_x = st["ep_dispatch_push"] + st["ep_dispatch_wait"]
+        comb_x = st["ep_combine_push"] + st["ep_combine_wait"]
+    else:
+        disp_names = ("ep_plan", "ep_dispatch_pack", "ep_dispatch_exchange", "ep_expert_permute")
+        comb_names = ("ep_combine_pack", "ep_combine_exchange", "ep_combine_reduce")
+        disp_x = st["ep_dispatch_exchange"]
+        comb_x = st["ep_combine_exchange"]
+    disp = sum(st[n] for n in disp_names)
+    comb = sum(st[n] for n in comb_names)
     per_rank = El
     own = torch.where((idx >= 0) & (idx < E), idx // per_rank, -1)
     off_slots = int(((own != rank) & (own >= 0)).sum().item())
@@ -603,6 +638,8 @@ def ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier):
     return {"workload": (f"cfg3: T={T} tokens per rank, E={E} over {world} rank(s), H={HIDDEN} "
                          "bf16, top-8 sigmoid routing (8 groups / 4 kept), synthetic bf16 expert "
                          "outputs, weighted per-slot combine with fp32 accumulation"),
+            "transport": "peer" if domain is not None else "nccl",
+            "stages_ms": st,
             "steps": steps,
             "dispatch_ms": disp, "combine_ms": comb,
             "dispatch_exchange_ms": disp_x, "combine_exchange_ms": comb_x,
@@ -630,6 +667,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep", action="store_true",
                     help="run the expert-parallel arm even on one GPU (default for N > 1)")
+    ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
+                    help="expert-parallel exchange: peer-memory kernels (default) or NCCL all-to-all")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)

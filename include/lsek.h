@@ -320,6 +320,84 @@ LSEK_API lsek_status lsek_ep_combine_reduce(void* out, const void* comb_rows,
                                    int32_t topk, int32_t hidden_dim, int32_t num_experts,
                                    int32_t world_size, void* stream);
 
+/* ---- expert-parallel over peer memory (NVLink) ---------------------------- */
+/* The same dispatch and combine with the exchanges done by the kernels
+ * themselves: every rank of one node allocates a symmetric buffer (a domain),
+ * the ranks swap its CUDA IPC handle once, and from then on the dispatch
+ * kernel stores token rows straight into the owner ranks' buffers and the
+ * down-projection GEMM stores each weighted per-slot row straight into the
+ * source rank's buffer, so the NVLink transfer overlaps the math.  Kernels
+ * publish with an epoch flag per rank; the waits are bounded (an expired wait
+ * records a device error, see lsek_device_error).  No counterpart in the
+ * reference (its consumer models the exchange as an all-reduce,
+ * tests/test_kernels.py:131-142, 187-200). */
+
+typedef struct lsek_ep_domain lsek_ep_domain;
+#define LSEK_EP_MAX_RANKS 16
+#define LSEK_EP_HANDLE_BYTES 64
+
+/* Bytes of one rank's symmetric buffer. */
+LSEK_API size_t lsek_ep_domain_bytes(int32_t max_tokens, int32_t hidden_dim, int32_t topk,
+                            int32_t world_size);
+/* Allocates this rank's buffer on the current device (zeroed). */
+LSEK_API lsek_status lsek_ep_domain_create(lsek_ep_domain** out, int32_t rank, int32_t world_size,
+                                  int32_t max_tokens, int32_t hidden_dim, int32_t topk);
+/* The CUDA IPC handle of this rank's buffer (LSEK_EP_HANDLE_BYTES). */
+LSEK_API lsek_status lsek_ep_domain_export(const lsek_ep_domain* d, void* handle,
+                                  size_t handle_bytes);
+/* Maps rank `peer`'s buffer from its exported handle. */
+LSEK_API lsek_status lsek_ep_domain_import(lsek_ep_domain* d, int32_t peer, const void* handle,
+                                  size_t handle_bytes);
+/* This rank's receive views: rows [cap_rows, H] bf16, ids / weights
+ * [cap_rows, topk], and the combine rows [cap_slots, H] bf16. */
+LSEK_API lsek_status lsek_ep_domain_buffers(const lsek_ep_domain* d, void** recv_rows,
+                                   int32_t** recv_ids, float** recv_w, void** back,
+                                   int64_t* cap_rows, int64_t* cap_slots);
+/* Synchronises the device, unmaps the peers and frees the buffer. */
+LSEK_API void lsek_ep_domain_destroy(lsek_ep_domain* d);
+
+/* Dispatch: stores each token row (and its per-slot local ids and weights)
+ * into the receive buffer of every rank owning one of its experts, writes
+ * the ids of the send rows to the local send_ids [send_capacity, topk], and
+ * publishes dispatch epoch `epoch` to every rank.  counts [G][G][2] (host)
+ * holds every rank's send_counts from lsek_ep_plan. */
+LSEK_API lsek_status lsek_ep_dispatch_push(lsek_ep_domain* d, int32_t* send_ids,
+                                  int32_t send_capacity, const int32_t* counts,
+                                  const void* hidden, const int32_t* topk_indices,
+                                  const float* topk_weights, const int32_t* pair_row,
+                                  const int32_t* send_off, int32_t num_tokens,
+                                  int32_t num_experts, uint32_t epoch, void* stream);
+/* Waits on the stream until every rank has published `epoch` for the
+ * dispatch (what = 0) or the combine (what = 1); gives up after timeout_ns
+ * (<= 0: 2 s) and records a device error. */
+LSEK_API lsek_status lsek_ep_wait(lsek_ep_domain* d, int32_t what, uint32_t epoch,
+                         int64_t timeout_ns, void* stream);
+/* Per permuted row of the received slots: the source rank, the row of its
+ * combine buffer and the weight (from the domain's recv ids / weights and
+ * the expert permute's src_to_dest_map; slot_row = lsek_ep_slot_scan of the
+ * received ids). */
+LSEK_API lsek_status lsek_ep_combine_plan(lsek_ep_domain* d, int32_t* dst_rank, int32_t* dst_row,
+                                 float* dst_w, const int32_t* src_to_dest_map,
+                                 const int32_t* slot_row, const int32_t* counts,
+                                 int32_t recv_rows, int32_t valid_slots, void* stream);
+/* The combine of expert outputs already in memory (no GEMM in front):
+ * bf16(dst_w[p] * expert_out[p]) to row dst_row[p] of rank dst_rank[p]'s
+ * combine buffer for p < rows, then publishes combine epoch `epoch`. */
+LSEK_API lsek_status lsek_ep_combine_push(lsek_ep_domain* d, const void* expert_out,
+                                 const int32_t* dst_rank, const int32_t* dst_row,
+                                 const float* dst_w, int32_t rows, uint32_t epoch,
+                                 void* stream);
+/* Down-projection GEMM with the combine fused into its epilogue: for each
+ * permuted row p, bf16(dst_w[p] * bf16(H[p] . W_down[e]^T)) goes to row
+ * dst_row[p] of rank dst_rank[p]'s combine buffer; then publishes combine
+ * epoch `epoch` to every rank.  H [rows, I] bf16, W_down [E_local, hidden, I]. */
+LSEK_API lsek_status lsek_ep_down_gemm_combine(lsek_ep_domain* d, const void* h, const void* w_down,
+                                      const int32_t* expert_offsets, int32_t local_experts,
+                                      int32_t rows, int32_t inter, const int32_t* dst_rank,
+                                      const int32_t* dst_row, const float* dst_w,
+                                      uint32_t epoch, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+
 /* ---- whole MoE layer ------------------------------------------------------ */
 
 /* Scratch bytes for lsek_moe_layer_forward. */

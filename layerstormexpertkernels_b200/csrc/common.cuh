@@ -54,13 +54,15 @@ cudaError_t once_per_device(PerDeviceOnce& once, F&& f) {
 // ---- device-side error word --------------------------------------------------
 
 // Codes a kernel records when its bounded wait expires; read back (and
-// cleared) by lsek_device_error.  The word itself lives in grouped_gemm.cu,
-// the translation unit of the only kernels that wait on one another.
+// cleared) by lsek_device_error.  Each translation unit with waiting kernels
+// keeps its own word (grouped_gemm.cu, ep.cu); lsek_device_error reads both.
 enum DeviceError : int32_t {
   kDevErrNone = 0,
   kDevErrGemmProducerWait = 1,
   kDevErrGemmMmaWait = 2,
   kDevErrGemmEpilogueWait = 3,
+  kDevErrEpDispatchWait = 4,   // a peer's dispatch rows did not arrive in time
+  kDevErrEpCombineWait = 5,    // a peer's combine slots did not arrive in time
 };
 
 // Nanoseconds since an arbitrary epoch (globaltimer); used to bound waits.

@@ -23,6 +23,7 @@
 //                       rank it places each outgoing slot
 //   combine rows [sum of valid slots, H] bf16(w * y), in received-row order
 #include "common.cuh"
+#include "ep_peer.cuh"
 
 namespace lsek {
 lsek_status launch_route(const int32_t* idx, int64_t n, int E, int32_t* offsets, int32_t* s2d,
@@ -254,7 +255,162 @@ __global__ void __launch_bounds__(kThreads) copy_valid_rows_kernel(
   }
 }
 
+// ---- peer-memory (NVLink) dispatch -------------------------------------------
+
+__device__ int32_t g_ep_error = 0;
+
+struct PushParams {
+  PeerTable peers;
+  int world, me;
+  int32_t dest_base[kMaxPeers];  // first row of this rank's rows in each destination's recv_rows
+  int64_t cap_rows;
+  size_t off_rows, off_ids, off_w;
+  uint32_t* done;
+  uint32_t epoch;
+};
+
+// One CTA per token (at least one CTA, so an empty rank still publishes):
+// the token's row is read once and stored into the recv_rows of every rank
+// that owns one of its experts, with the per-slot local ids and weights; the
+// ids also go to the local send_ids (the sender's combine needs them).
+__global__ void __launch_bounds__(kThreads) ep_dispatch_push_kernel(
+    const __grid_constant__ PushParams pp, int32_t* __restrict__ send_ids, int32_t capacity,
+    const uint4* __restrict__ hidden, const int32_t* __restrict__ idx, const float* __restrict__ w,
+    const int32_t* __restrict__ pair_row, const int32_t* __restrict__ send_off, int T, int k,
+    int64_t vec_per_row, int E) {
+  __shared__ int32_t s_row[kMaxPeers];   // send row (global index), or -1
+  __shared__ int64_t s_dst[kMaxPeers];   // row in the destination's recv_rows
+  const int t = blockIdx.x;
+  const int G = pp.world;
+  if (t < T) {
+    const int32_t rows = min(__ldg(send_off + G), capacity);
+    const int per = E / G;
+    if (threadIdx.x < G) {
+      const int g = threadIdx.x;
+      const int32_t row = __ldg(pair_row + static_cast<int64_t>(t) * G + g);
+      const int64_t dst = pp.dest_base[g] + static_cast<int64_t>(row - __ldg(send_off + g));
+      const bool ok = row < rows && dst >= 0 && dst < pp.cap_rows;
+      s_row[g] = ok ? row : -1;
+      s_dst[g] = dst;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * k; i += kThreads) {
+      const int g = i / k, j = i - (i / k) * k;
+      if (s_row[g] < 0) continue;
+      const int32_t e = __ldg(idx + static_cast<int64_t>(t) * k + j);
+      const bool mine = owned_by(e, E, per, g);
+      const int32_t id = mine ? e - g * per : -1;
+      const float wt = mine ? __ldg(w + static_cast<int64_t>(t) * k + j) : 0.0f;
+      char* base = pp.peers.base[g];
+      reinterpret_cast<int32_t*>(base + pp.off_ids)[s_dst[g] * k + j] = id;
+      reinterpret_cast<float*>(base + pp.off_w)[s_dst[g] * k + j] = wt;
+      send_ids[static_cast<int64_t>(s_row[g]) * k + j] = id;
+    }
+    const uint4* src = hidden + static_cast<int64_t>(t) * vec_per_row;
+    for (int64_t v0 = threadIdx.x; v0 < vec_per_row; v0 += kThreads * 4) {
+      uint4 r[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t v = v0 + i * kThreads;
+        if (v < vec_per_row) r[i] = ldg_nc_v4(src + v);
+      }
+      for (int g = 0; g < G; ++g) {
+        if (s_row[g] < 0) continue;
+        uint4* dst = reinterpret_cast<uint4*>(pp.peers.base[g] + pp.off_rows) + s_dst[g] * vec_per_row;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int64_t v = v0 + i * kThreads;
+          if (v < vec_per_row) dst[v] = r[i];
+        }
+      }
+    }
+  }
+  grid_release_to_peers(pp.peers, G, pp.me, kCtrlDispatchFlags, pp.done, pp.epoch);
+}
+
+// Thread g waits until flags[g] has reached `epoch` (wrap-safe compare), at
+// most limit_ns; on expiry it records `code` and returns.
+__global__ void ep_wait_kernel(const uint32_t* flags, int G, uint32_t epoch, uint64_t limit_ns,
+                               int32_t code) {
+  const int g = threadIdx.x;
+  if (g >= G) return;
+  const uint64_t t0 = global_ns();
+  while (static_cast<int32_t>(ld_acquire_sys(flags + g) - epoch) < 0) {
+    if (global_ns() - t0 > limit_ns) {
+      atomicCAS(&g_ep_error, 0, code);
+      return;
+    }
+    __nanosleep(100);
+  }
+}
+
+struct RecvSplit {
+  int32_t recv_start[kMaxPeers + 1];  // first received row of each source
+  int32_t back_base[kMaxPeers];       // first row of this rank's part in each source's back buffer
+};
+
+// Per permuted row p (a valid received slot): the source rank, the row of
+// its back buffer that receives bf16(w * y[p]), and w.
+__global__ void ep_combine_plan_kernel(int32_t* __restrict__ dst_rank, int32_t* __restrict__ dst_row,
+                                       float* __restrict__ dst_w, const int32_t* __restrict__ ids,
+                                       const float* __restrict__ w, const int32_t* __restrict__ s2d,
+                                       const int32_t* __restrict__ slot_row,
+                                       const __grid_constant__ RecvSplit sp, int R, int k, int G,
+                                       int32_t valid) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i >= static_cast<int64_t>(R) * k) return;
+  if (__ldg(ids + i) < 0) return;
+  const int r = static_cast<int>(i / k), j = static_cast<int>(i - static_cast<int64_t>(r) * k);
+  int src = 0;
+  while (src + 1 < G && sp.recv_start[src + 1] <= r) ++src;
+  int rank = 0;
+  for (int jj = 0; jj < j; ++jj) rank += __ldg(ids + static_cast<int64_t>(r) * k + jj) >= 0;
+  const int32_t p = __ldg(s2d + i);
+  if (p < 0 || p >= valid) return;
+  dst_rank[p] = src;
+  dst_row[p] = sp.back_base[src] + (__ldg(slot_row + r) - __ldg(slot_row + sp.recv_start[src])) + rank;
+  dst_w[p] = __ldg(w + i);
+}
+
+// The combine without a GEMM in front (expert outputs already in memory):
+// row p of y becomes bf16(dst_w[p] * y[p]) at row dst_row[p] of rank
+// dst_rank[p]'s combine buffer; the last CTA publishes the combine epoch.
+__global__ void __launch_bounds__(kThreads) ep_combine_push_kernel(
+    const __grid_constant__ PeerTable peers, size_t back_off, const __nv_bfloat16* __restrict__ y,
+    const int32_t* __restrict__ dst_rank, const int32_t* __restrict__ dst_row,
+    const float* __restrict__ dst_w, int32_t rows, int64_t cap_slots, int H, int world, int me,
+    uint32_t* done, uint32_t epoch) {
+  const int nvec = H / 8;
+  for (int32_t p = blockIdx.x; p < rows; p += gridDim.x) {
+    const int32_t rk = __ldg(dst_rank + p);
+    const int32_t dr = __ldg(dst_row + p);
+    if (rk < 0 || rk >= world || dr < 0 || dr >= cap_slots) continue;
+    const float wt = __ldg(dst_w + p);
+    const __nv_bfloat16* src = y + static_cast<int64_t>(p) * H;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peers.base[rk] + back_off) +
+                         static_cast<int64_t>(dr) * H;
+    for (int v = threadIdx.x; v < nvec; v += kThreads) {
+      const uint4 raw = ldg_nc_v4(src + v * 8);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+      uint4 out;
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(&out);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o[q] = __float2bfloat16_rn(__fmul_rn(wt, __bfloat162float(e[q])));
+      *reinterpret_cast<uint4*>(dst + v * 8) = out;
+    }
+  }
+  grid_release_to_peers(peers, world, me, kCtrlCombineFlags, done, epoch);
+}
+
 }  // namespace
+
+lsek_status ep_take_device_error(int32_t* code) {
+  int32_t zero = 0;
+  LSEK_CUDA_TRY(cudaMemcpyFromSymbol(code, g_ep_error, sizeof(int32_t)));
+  LSEK_CUDA_TRY(cudaMemcpyToSymbol(g_ep_error, &zero, sizeof(int32_t)));
+  return LSEK_OK;
+}
+
 }  // namespace lsek
 
 using namespace lsek;
@@ -408,4 +564,233 @@ extern "C" lsek_status lsek_ep_combine_reduce(void* out, const void* comb_rows,
       static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(comb_rows), topk_indices,
       pair_row, slot_row, comb_count, topk, hidden_dim, num_experts, world_size, span);
   return check_launch("ep_combine_reduce");
+}
+
+// ---- peer domain -----------------------------------------------------------------
+
+static lsek_status domain_check(const lsek_ep_domain* h, const char* name) {
+  LSEK_REQUIRE(h != nullptr, "%s: domain is NULL", name);
+  for (int g = 0; g < h->d.world; ++g)
+    LSEK_REQUIRE(h->d.peer[g] != nullptr, "%s: rank %d of the domain has not been imported", name, g);
+  int dev = -1;
+  LSEK_CUDA_TRY(cudaGetDevice(&dev));
+  LSEK_REQUIRE(dev == h->d.device, "%s: the domain lives on device %d, current device is %d", name,
+               h->d.device, dev);
+  return LSEK_OK;
+}
+
+// counts [G][G][2]: row s = (rows, slots) source s sends to each rank.
+static int64_t col_sum(const int32_t* counts, int G, int upto_s, int g, int c) {
+  int64_t v = 0;
+  for (int s = 0; s < upto_s; ++s) v += counts[(static_cast<int64_t>(s) * G + g) * 2 + c];
+  return v;
+}
+
+extern "C" size_t lsek_ep_domain_bytes(int32_t max_tokens, int32_t hidden_dim, int32_t topk,
+                                       int32_t world_size) {
+  if (max_tokens < 0 || hidden_dim <= 0 || topk <= 0 || world_size <= 0) return 0;
+  return ep_layout(max_tokens, hidden_dim, topk, world_size).total;
+}
+
+extern "C" lsek_status lsek_ep_domain_create(lsek_ep_domain** out, int32_t rank, int32_t world_size,
+                                             int32_t max_tokens, int32_t hidden_dim, int32_t topk) {
+  LSEK_REQUIRE(out != nullptr, "ep_domain_create: out is NULL");
+  *out = nullptr;
+  LSEK_REQUIRE(world_size >= 1 && world_size <= kMaxPeers,
+               "ep_domain_create: world size must be in [1, %d]", kMaxPeers);
+  LSEK_REQUIRE(rank >= 0 && rank < world_size, "ep_domain_create: rank out of range");
+  LSEK_REQUIRE(max_tokens >= 1 && hidden_dim > 0 && hidden_dim % 8 == 0 && topk >= 1 && topk <= 32,
+               "ep_domain_create: bad sizes");
+  auto* h = new lsek_ep_domain();
+  EpDomain& d = h->d;
+  d.rank = rank;
+  d.world = world_size;
+  d.max_tokens = max_tokens;
+  d.H = hidden_dim;
+  d.k = topk;
+  d.lay = ep_layout(max_tokens, hidden_dim, topk, world_size);
+  d.local = nullptr;
+  for (int g = 0; g < kMaxPeers; ++g) {
+    d.peer[g] = nullptr;
+    d.imported[g] = false;
+  }
+  cudaError_t e = cudaGetDevice(&d.device);
+  if (e == cudaSuccess) e = cudaMalloc(&d.local, d.lay.total);
+  if (e == cudaSuccess) e = cudaMemset(d.local, 0, d.lay.total);
+  if (e != cudaSuccess) {
+    if (d.local) cudaFree(d.local);
+    delete h;
+    return fail(LSEK_ERR_CUDA, "ep_domain_create: %s", cudaGetErrorString(e));
+  }
+  d.peer[rank] = d.local;
+  *out = h;
+  return LSEK_OK;
+}
+
+extern "C" lsek_status lsek_ep_domain_export(const lsek_ep_domain* h, void* handle,
+                                             size_t handle_bytes) {
+  LSEK_REQUIRE(h != nullptr && handle != nullptr, "ep_domain_export: NULL argument");
+  LSEK_REQUIRE(handle_bytes >= sizeof(cudaIpcMemHandle_t),
+               "ep_domain_export: handle buffer needs %zu bytes", sizeof(cudaIpcMemHandle_t));
+  cudaIpcMemHandle_t ipc;
+  LSEK_CUDA_TRY(cudaIpcGetMemHandle(&ipc, h->d.local));
+  std::memcpy(handle, &ipc, sizeof(ipc));
+  return LSEK_OK;
+}
+
+extern "C" lsek_status lsek_ep_domain_import(lsek_ep_domain* h, int32_t peer, const void* handle,
+                                             size_t handle_bytes) {
+  LSEK_REQUIRE(h != nullptr && handle != nullptr, "ep_domain_import: NULL argument");
+  EpDomain& d = h->d;
+  LSEK_REQUIRE(peer >= 0 && peer < d.world, "ep_domain_import: peer out of range");
+  LSEK_REQUIRE(handle_bytes >= sizeof(cudaIpcMemHandle_t), "ep_domain_import: short handle");
+  if (peer == d.rank) return LSEK_OK;
+  LSEK_REQUIRE(d.peer[peer] == nullptr, "ep_domain_import: rank %d already imported", peer);
+  cudaIpcMemHandle_t ipc;
+  std::memcpy(&ipc, handle, sizeof(ipc));
+  void* ptr = nullptr;
+  LSEK_CUDA_TRY(cudaIpcOpenMemHandle(&ptr, ipc, cudaIpcMemLazyEnablePeerAccess));
+  d.peer[peer] = static_cast<char*>(ptr);
+  d.imported[peer] = true;
+  return LSEK_OK;
+}
+
+extern "C" lsek_status lsek_ep_domain_buffers(const lsek_ep_domain* h, void** recv_rows,
+                                              int32_t** recv_ids, float** recv_w, void** back,
+                                              int64_t* cap_rows, int64_t* cap_slots) {
+  LSEK_REQUIRE(h != nullptr, "ep_domain_buffers: domain is NULL");
+  const EpDomain& d = h->d;
+  if (recv_rows) *recv_rows = d.local + d.lay.recv_rows;
+  if (recv_ids) *recv_ids = reinterpret_cast<int32_t*>(d.local + d.lay.recv_ids);
+  if (recv_w) *recv_w = reinterpret_cast<float*>(d.local + d.lay.recv_w);
+  if (back) *back = d.local + d.lay.back;
+  if (cap_rows) *cap_rows = d.lay.cap_rows;
+  if (cap_slots) *cap_slots = d.lay.cap_slots;
+  return LSEK_OK;
+}
+
+extern "C" void lsek_ep_domain_destroy(lsek_ep_domain* h) {
+  if (h == nullptr) return;
+  EpDomain& d = h->d;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(d.device);
+  cudaDeviceSynchronize();
+  for (int g = 0; g < d.world; ++g)
+    if (d.imported[g] && d.peer[g]) cudaIpcCloseMemHandle(d.peer[g]);
+  if (d.local) cudaFree(d.local);
+  if (prev >= 0) cudaSetDevice(prev);
+  delete h;
+}
+
+extern "C" lsek_status lsek_ep_dispatch_push(lsek_ep_domain* h, int32_t* send_ids,
+                                             int32_t send_capacity, const int32_t* counts,
+                                             const void* hidden, const int32_t* topk_indices,
+                                             const float* topk_weights, const int32_t* pair_row,
+                                             const int32_t* send_off, int32_t num_tokens,
+                                             int32_t num_experts, uint32_t epoch, void* stream) {
+  lsek_status s = domain_check(h, "ep_dispatch_push");
+  if (s != LSEK_OK) return s;
+  const EpDomain& d = h->d;
+  const int G = d.world;
+  s = ep_check(num_tokens, static_cast<int>(d.k), num_experts, G, "ep_dispatch_push");
+  if (s != LSEK_OK) return s;
+  LSEK_REQUIRE(num_tokens <= d.max_tokens, "ep_dispatch_push: %d tokens exceed the domain's %lld",
+               num_tokens, static_cast<long long>(d.max_tokens));
+  LSEK_REQUIRE(counts != nullptr && send_capacity >= 0, "ep_dispatch_push: bad counts / capacity");
+  LSEK_REQUIRE(num_tokens == 0 || (hidden && topk_indices && topk_weights && pair_row && send_off &&
+                                   (send_capacity == 0 || send_ids)),
+               "ep_dispatch_push: NULL tensor pointer");
+  PushParams pp;
+  pp.peers = peer_table(d);
+  pp.world = G;
+  pp.me = d.rank;
+  for (int g = 0; g < kMaxPeers; ++g) pp.dest_base[g] = 0;
+  for (int g = 0; g < G; ++g) {
+    const int64_t base = col_sum(counts, G, d.rank, g, 0);
+    const int64_t total = col_sum(counts, G, G, g, 0);
+    LSEK_REQUIRE(total <= d.lay.cap_rows, "ep_dispatch_push: rank %d would receive %lld rows (capacity %lld)",
+                 g, static_cast<long long>(total), static_cast<long long>(d.lay.cap_rows));
+    pp.dest_base[g] = static_cast<int32_t>(base);
+  }
+  pp.cap_rows = d.lay.cap_rows;
+  pp.off_rows = d.lay.recv_rows;
+  pp.off_ids = d.lay.recv_ids;
+  pp.off_w = d.lay.recv_w;
+  pp.done = reinterpret_cast<uint32_t*>(d.local + kCtrlPushDone);
+  pp.epoch = epoch;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  LSEK_CUDA_TRY(cudaMemsetAsync(pp.done, 0, sizeof(uint32_t), st));
+  ep_dispatch_push_kernel<<<num_tokens > 0 ? num_tokens : 1, kThreads, 0, st>>>(
+      pp, send_ids, send_capacity, static_cast<const uint4*>(hidden), topk_indices, topk_weights,
+      pair_row, send_off, num_tokens, static_cast<int>(d.k), d.H / 8, num_experts);
+  return check_launch("ep_dispatch_push");
+}
+
+extern "C" lsek_status lsek_ep_wait(lsek_ep_domain* h, int32_t what, uint32_t epoch,
+                                    int64_t timeout_ns, void* stream) {
+  lsek_status s = domain_check(h, "ep_wait");
+  if (s != LSEK_OK) return s;
+  LSEK_REQUIRE(what == 0 || what == 1, "ep_wait: what must be 0 (dispatch) or 1 (combine)");
+  const EpDomain& d = h->d;
+  const uint32_t* flags =
+      reinterpret_cast<const uint32_t*>(d.local + (what == 0 ? kCtrlDispatchFlags : kCtrlCombineFlags));
+  const uint64_t limit = timeout_ns > 0 ? static_cast<uint64_t>(timeout_ns) : kWaitLimitNs;
+  ep_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      flags, d.world, epoch, limit, what == 0 ? kDevErrEpDispatchWait : kDevErrEpCombineWait);
+  return check_launch("ep_wait");
+}
+
+extern "C" lsek_status lsek_ep_combine_plan(lsek_ep_domain* h, int32_t* dst_rank, int32_t* dst_row,
+                                            float* dst_w, const int32_t* src_to_dest_map,
+                                            const int32_t* slot_row, const int32_t* counts,
+                                            int32_t recv_rows, int32_t valid_slots, void* stream) {
+  lsek_status s = domain_check(h, "ep_combine_plan");
+  if (s != LSEK_OK) return s;
+  const EpDomain& d = h->d;
+  const int G = d.world;
+  LSEK_REQUIRE(counts != nullptr, "ep_combine_plan: counts is NULL");
+  LSEK_REQUIRE(recv_rows >= 0 && recv_rows <= d.lay.cap_rows && valid_slots >= 0,
+               "ep_combine_plan: bad sizes");
+  RecvSplit sp;
+  for (int g = 0; g <= kMaxPeers; ++g) sp.recv_start[g] = 0;
+  for (int g = 0; g < kMaxPeers; ++g) sp.back_base[g] = 0;
+  for (int src = 0; src <= G; ++src) sp.recv_start[src] = static_cast<int32_t>(col_sum(counts, G, src, d.rank, 0));
+  LSEK_REQUIRE(sp.recv_start[G] == recv_rows, "ep_combine_plan: recv_rows disagrees with counts");
+  for (int src = 0; src < G; ++src) {
+    int64_t b = 0;
+    for (int g = 0; g < d.rank; ++g) b += counts[(static_cast<int64_t>(src) * G + g) * 2 + 1];
+    sp.back_base[src] = static_cast<int32_t>(b);
+  }
+  const int64_t n = static_cast<int64_t>(recv_rows) * d.k;
+  if (n == 0 || valid_slots == 0) return LSEK_OK;
+  LSEK_REQUIRE(dst_rank && dst_row && dst_w && src_to_dest_map && slot_row,
+               "ep_combine_plan: NULL tensor pointer");
+  ep_combine_plan_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0,
+                           static_cast<cudaStream_t>(stream)>>>(
+      dst_rank, dst_row, dst_w, reinterpret_cast<const int32_t*>(d.local + d.lay.recv_ids),
+      reinterpret_cast<const float*>(d.local + d.lay.recv_w), src_to_dest_map, slot_row, sp,
+      recv_rows, static_cast<int>(d.k), G, valid_slots);
+  return check_launch("ep_combine_plan");
+}
+
+extern "C" lsek_status lsek_ep_combine_push(lsek_ep_domain* h, const void* expert_out,
+                                            const int32_t* dst_rank, const int32_t* dst_row,
+                                            const float* dst_w, int32_t rows, uint32_t epoch,
+                                            void* stream) {
+  lsek_status s = domain_check(h, "ep_combine_push");
+  if (s != LSEK_OK) return s;
+  const EpDomain& d = h->d;
+  LSEK_REQUIRE(rows >= 0, "ep_combine_push: bad row count");
+  LSEK_REQUIRE(rows == 0 || (expert_out && dst_rank && dst_row && dst_w),
+               "ep_combine_push: NULL tensor pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t* done = reinterpret_cast<uint32_t*>(d.local + kCtrlGemmDone);
+  LSEK_CUDA_TRY(cudaMemsetAsync(done, 0, sizeof(uint32_t), st));
+  const int64_t want = 4ll * num_sms();
+  const unsigned grid = static_cast<unsigned>(rows == 0 ? 1 : (rows < want ? rows : want));
+  ep_combine_push_kernel<<<grid, kThreads, 0, st>>>(
+      peer_table(d), d.lay.back, static_cast<const __nv_bfloat16*>(expert_out), dst_rank, dst_row,
+      dst_w, rows, d.lay.cap_slots, static_cast<int>(d.H), d.world, d.rank, done, epoch);
+  return check_launch("ep_combine_push");
 }

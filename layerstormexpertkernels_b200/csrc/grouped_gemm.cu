@@ -39,6 +39,12 @@
 // with r instead of a full 128-row tile.  The epilogue of such a tile reads
 // the transposed accumulator (TMEM lane = output column, TMEM column =
 // token).  The same products are summed in the same k order either way.
+// COMBINE mode (the expert-parallel down projection) ends each output row
+// in the combine instead of D: row p becomes bf16(w[p] * bf16(acc)) stored at
+// row dst_row[p] of rank dst_rank[p]'s combine buffer (peer memory over
+// NVLink), and the last CTA publishes the combine epoch to every rank.  The
+// per-element arithmetic is that of the plain GEMM followed by
+// moe_unpermute_bf16_perslot.
 // SWIGLU mode stacks 128 gate rows (rows n*128 of the expert) and the matching
 // 128 up rows (rows I + n*128) as the two B boxes, so one N=256 MMA yields g
 // and u for 128 output columns; the epilogue rounds both to bf16 and applies
@@ -54,9 +60,12 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "ep_peer.cuh"
 #include "swiglu.cuh"
 
 namespace lsek {
+
+lsek_status ep_take_device_error(int32_t* code);  // ep.cu
 
 // Device-side error word (see DeviceError in common.cuh).
 __device__ int32_t g_device_error = 0;
@@ -103,7 +112,19 @@ struct Params {
   int n_out;               // output width
   float swiglu_limit;
   int32_t* counter;        // zeroed unit counter in device memory, or null (static stride)
+  // COMBINE mode
+  const int32_t* dst_rank;  // [rows] rank whose combine buffer receives row p
+  const int32_t* dst_row;   // [rows] row there
+  const float* dst_w;       // [rows] routing weight
+  PeerTable peers;          // every rank's domain buffer
+  size_t back_offset;       // combine buffer offset inside a domain buffer
+  int64_t back_rows;        // rows of each rank's combine buffer (larger dst_row: skipped)
+  int world, me;
+  uint32_t* done;           // zeroed local CTA counter
+  uint32_t epoch;
 };
+
+enum GemmMode : int { kModePlain = 0, kModeSwiglu = 1, kModeCombine = 2 };
 
 struct Smem {
   uint8_t tiles[kStages][kStageBytes];  // 1024-byte aligned (base is aligned)
@@ -280,10 +301,12 @@ __device__ __forceinline__ void decode_unit(const Smem& s, int num_experts, int 
   m = local - n * mt;
 }
 
-template <bool SWIGLU>
+template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                        const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+                        const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ Params p) {
+  constexpr bool SWIGLU = MODE == kModeSwiglu;
+  constexpr bool COMBINE = MODE == kModeCombine;
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~static_cast<uintptr_t>(1023));
@@ -506,14 +529,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kBN);
       const int col0 = n * p.out_tile_cols;
       const int cols_here = min(p.out_tile_cols, p.n_out - col0);
-      __nv_bfloat16* drow = p.D + static_cast<int64_t>(valid ? r : 0) * p.ldd + col0;
+      __nv_bfloat16* drow = nullptr;
+      float wrow = 1.0f;
+      bool live = valid;
+      if (COMBINE) {
+        if (valid) {
+          const int32_t rk = __ldg(p.dst_rank + r), dr = __ldg(p.dst_row + r);
+          live = rk >= 0 && rk < p.world && dr >= 0 && dr < p.back_rows;
+          if (live)
+            drow = reinterpret_cast<__nv_bfloat16*>(p.peers.base[rk] + p.back_offset) +
+                   static_cast<int64_t>(dr) * p.ldd + col0;
+          wrow = __ldg(p.dst_w + r);
+        }
+      } else {
+        drow = p.D + static_cast<int64_t>(valid ? r : 0) * p.ldd + col0;
+      }
       if (rows_here <= kSwapMaxRows) {
         // Transposed accumulator: this thread's TMEM lane is weight row
         // w = 32q + lane of each box, columns [0, nn) hold box 0 for the
         // tile's tokens and [nn, 2nn) box 1.
         const int nn = (rows_here + 15) & ~15;
         const int w = q * 32 + lane;
-        __nv_bfloat16* dcol = p.D + static_cast<int64_t>(row0) * p.ldd + col0;
+        __nv_bfloat16* dcol = COMBINE ? nullptr : p.D + static_cast<int64_t>(row0) * p.ldd + col0;
 #pragma unroll 1
         for (int t0 = 0; t0 < nn; t0 += 16) {
           uint32_t v0[16], v1[16];
@@ -524,6 +561,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 16; ++i) {
             const int t = t0 + i;
             if (t >= rows_here) break;
+            if (COMBINE) {
+              const int pr = row0 + t;
+              const int32_t rk = __ldg(p.dst_rank + pr), dr = __ldg(p.dst_row + pr);
+              if (rk < 0 || rk >= p.world || dr < 0 || dr >= p.back_rows) continue;
+              __nv_bfloat16* dst =
+                  reinterpret_cast<__nv_bfloat16*>(p.peers.base[rk] + p.back_offset) +
+                  static_cast<int64_t>(dr) * p.ldd + col0;
+              const float wt = __ldg(p.dst_w + pr);
+              if (w < cols_here)
+                dst[w] = __float2bfloat16_rn(__fmul_rn(wt, round_bf16(__uint_as_float(v0[i]))));
+              if (kBoxRows + w < cols_here)
+                dst[kBoxRows + w] =
+                    __float2bfloat16_rn(__fmul_rn(wt, round_bf16(__uint_as_float(v1[i]))));
+              continue;
+            }
             __nv_bfloat16* dst = dcol + static_cast<int64_t>(t) * p.ldd;
             if (SWIGLU) {
               if (w < cols_here)
@@ -568,11 +620,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t v[32];
           tmem_ld32(tbase + c, v);
           tmem_ld_wait();
-          if (valid && c < cols_here) {
+          if (live && c < cols_here) {
             uint32_t packed[16];
+            if (COMBINE) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              packed[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+              for (int j = 0; j < 16; ++j)
+                packed[j] = pack_bf16x2(__fmul_rn(wrow, round_bf16(__uint_as_float(v[2 * j]))),
+                                        __fmul_rn(wrow, round_bf16(__uint_as_float(v[2 * j + 1]))));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                packed[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+            }
             uint4* dst = reinterpret_cast<uint4*>(drow + c);
 #pragma unroll
             for (int j = 0; j < 4; ++j)
@@ -595,6 +654,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                  "r"(kTmemCols)
                  : "memory");
   }
+  if (COMBINE) grid_release_to_peers(p.peers, p.world, p.me, kCtrlCombineFlags, p.done, p.epoch);
+}
+
+// Publishes the combine epoch when a rank has no rows to multiply.
+__global__ void combine_release_kernel(const __grid_constant__ Params p) {
+  grid_release_to_peers(p.peers, p.world, p.me, kCtrlCombineFlags, p.done, p.epoch);
 }
 
 // ---- host side -----------------------------------------------------------------
@@ -636,12 +701,14 @@ lsek_status make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_
   return LSEK_OK;
 }
 
-template <bool SWIGLU>
+template <int MODE>
 lsek_status launch(void* D, const void* A, const void* B, const int32_t* offsets, int E, int rows,
-                   int n_out, int b_rows, int K, float limit, int32_t* counter, cudaStream_t st) {
+                   int n_out, int b_rows, int K, float limit, int32_t* counter, cudaStream_t st,
+                   const Params* combine = nullptr) {
+  constexpr bool SWIGLU = MODE == kModeSwiglu;
   static PerDeviceOnce attrs;
   const cudaError_t ae = once_per_device(attrs, [] {
-    return cudaFuncSetAttribute(grouped_gemm_kernel<SWIGLU>,
+    return cudaFuncSetAttribute(grouped_gemm_kernel<MODE>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(kSmemBytes));
   });
@@ -652,6 +719,7 @@ lsek_status launch(void* D, const void* A, const void* B, const int32_t* offsets
   s = make_map(&mb, B, static_cast<uint64_t>(K), static_cast<uint64_t>(E) * b_rows);
   if (s != LSEK_OK) return s;
   Params p;
+  if (combine != nullptr) p = *combine;
   p.offsets = offsets;
   p.num_experts = E;
   p.rows = rows;
@@ -676,8 +744,10 @@ lsek_status launch(void* D, const void* A, const void* B, const int32_t* offsets
   }
   const int64_t max_units = (ceil_div(rows, kBM) + E) * static_cast<int64_t>(p.n_tiles);
   const int grid = static_cast<int>(max_units < num_sms() ? max_units : num_sms());
-  grouped_gemm_kernel<SWIGLU><<<grid, kThreads, kSmemBytes, st>>>(ma, mb, p);
-  return check_launch(SWIGLU ? "grouped_gemm_swiglu_bf16" : "grouped_gemm_bf16");
+  if (MODE == kModeCombine) LSEK_CUDA_TRY(cudaMemsetAsync(p.done, 0, sizeof(uint32_t), st));
+  grouped_gemm_kernel<MODE><<<grid, kThreads, kSmemBytes, st>>>(ma, mb, p);
+  return check_launch(SWIGLU ? "grouped_gemm_swiglu_bf16"
+                             : (MODE == kModeCombine ? "ep_down_gemm_combine" : "grouped_gemm_bf16"));
 }
 
 lsek_status validate(const char* name, const void* D, const void* A, const void* B,
@@ -703,13 +773,13 @@ lsek_status validate(const char* name, const void* D, const void* A, const void*
 lsek_status grouped_gemm_plain(void* D, const void* A, const void* B, const int32_t* offsets, int E,
                                int rows, int N, int K, int32_t* counter, cudaStream_t st) {
   if (rows == 0 || N == 0) return LSEK_OK;
-  return gemm::launch<false>(D, A, B, offsets, E, rows, N, N, K, 0.0f, counter, st);
+  return gemm::launch<gemm::kModePlain>(D, A, B, offsets, E, rows, N, N, K, 0.0f, counter, st);
 }
 lsek_status grouped_gemm_swiglu(void* H, const void* A, const void* Wgu, const int32_t* offsets,
                                 int E, int rows, int I, int K, float limit, int32_t* counter,
                                 cudaStream_t st) {
   if (rows == 0 || I == 0) return LSEK_OK;
-  return gemm::launch<true>(H, A, Wgu, offsets, E, rows, I, 2 * I, K, limit, counter, st);
+  return gemm::launch<gemm::kModeSwiglu>(H, A, Wgu, offsets, E, rows, I, 2 * I, K, limit, counter, st);
 }
 
 }  // namespace lsek
@@ -722,6 +792,10 @@ extern "C" lsek_status lsek_device_error(int32_t* code, void* stream) {
   int32_t zero = 0;
   LSEK_CUDA_TRY(cudaMemcpyFromSymbol(code, g_device_error, sizeof(int32_t)));
   LSEK_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int32_t)));
+  int32_t ep_code = 0;
+  const lsek_status s = ep_take_device_error(&ep_code);
+  if (s != LSEK_OK) return s;
+  if (*code == 0) *code = ep_code;
   return LSEK_OK;
 }
 
@@ -763,4 +837,47 @@ extern "C" lsek_status lsek_grouped_gemm_swiglu_bf16(void* Hout, const void* A, 
   return grouped_gemm_swiglu(Hout, A, W_gu, expert_offsets, num_experts, rows, I, K, swiglu_limit,
                              gemm_counter(workspace, workspace_bytes),
                              static_cast<cudaStream_t>(stream));
+}
+
+extern "C" lsek_status lsek_ep_down_gemm_combine(lsek_ep_domain* h, const void* hact,
+                                                 const void* w_down, const int32_t* expert_offsets,
+                                                 int32_t local_experts, int32_t rows, int32_t inter,
+                                                 const int32_t* dst_rank, const int32_t* dst_row,
+                                                 const float* dst_w, uint32_t epoch,
+                                                 void* workspace, size_t workspace_bytes,
+                                                 void* stream) {
+  using namespace lsek;
+  LSEK_REQUIRE(h != nullptr, "ep_down_gemm_combine: domain is NULL");
+  const EpDomain& d = h->d;
+  for (int g = 0; g < d.world; ++g)
+    LSEK_REQUIRE(d.peer[g] != nullptr, "ep_down_gemm_combine: rank %d has not been imported", g);
+  const int H = static_cast<int>(d.H);
+  lsek_status s = gemm::validate("ep_down_gemm_combine", d.local, hact, w_down, expert_offsets,
+                                 local_experts, rows, H, inter);
+  if (s != LSEK_OK) return s;
+  LSEK_REQUIRE(static_cast<int64_t>(local_experts) * H < (1ll << 31),
+               "ep_down_gemm_combine: local_experts * hidden must fit in int32");
+  LSEK_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 4 == 0,
+               "ep_down_gemm_combine: workspace must be 4-byte aligned");
+  gemm::Params cp{};
+  cp.dst_rank = dst_rank;
+  cp.dst_row = dst_row;
+  cp.dst_w = dst_w;
+  cp.peers = peer_table(d);
+  cp.back_offset = d.lay.back;
+  cp.back_rows = d.lay.cap_slots;
+  cp.world = d.world;
+  cp.me = d.rank;
+  cp.done = reinterpret_cast<uint32_t*>(d.local + kCtrlGemmDone);
+  cp.epoch = epoch;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rows == 0 || inter == 0) {
+    LSEK_CUDA_TRY(cudaMemsetAsync(cp.done, 0, sizeof(uint32_t), st));
+    gemm::combine_release_kernel<<<1, 32, 0, st>>>(cp);
+    return check_launch("ep_down_gemm_combine(release)");
+  }
+  LSEK_REQUIRE(dst_rank && dst_row && dst_w, "ep_down_gemm_combine: NULL plan pointer");
+  return gemm::launch<gemm::kModeCombine>(nullptr, hact, w_down, expert_offsets, local_experts,
+                                          rows, H, H, inter, 0.0f,
+                                          gemm_counter(workspace, workspace_bytes), st, &cp);
 }

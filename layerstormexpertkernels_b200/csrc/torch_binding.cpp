@@ -501,6 +501,145 @@ torch::Tensor ep_combine_reduce(torch::Tensor comb_rows, torch::Tensor topk_indi
   return out;
 }
 
+// ---- expert-parallel peer domain (handles travel as Python ints) --------------
+
+lsek_ep_domain* domain_of(int64_t h) {
+  TORCH_CHECK(h != 0, "ep domain handle is null");
+  return reinterpret_cast<lsek_ep_domain*>(static_cast<intptr_t>(h));
+}
+
+void check_counts(const torch::Tensor& counts) {
+  TORCH_CHECK(!counts.is_cuda() && counts.is_contiguous() && counts.scalar_type() == at::kInt &&
+                  counts.dim() == 3 && counts.size(2) == 2,
+              "counts must be a contiguous int32 CPU tensor [G, G, 2]");
+}
+
+int64_t ep_domain_create(int64_t rank, int64_t world_size, int64_t max_tokens, int64_t hidden_dim,
+                         int64_t topk) {
+  lsek_ep_domain* d = nullptr;
+  check_status(lsek_ep_domain_create(&d, to_i32(rank, "rank"), to_i32(world_size, "world_size"),
+                                     to_i32(max_tokens, "max_tokens"), to_i32(hidden_dim, "hidden"),
+                                     to_i32(topk, "topk")));
+  return static_cast<int64_t>(reinterpret_cast<intptr_t>(d));
+}
+
+torch::Tensor ep_domain_export(int64_t h) {
+  auto out = torch::empty({LSEK_EP_HANDLE_BYTES}, torch::dtype(torch::kUInt8));
+  check_status(lsek_ep_domain_export(domain_of(h), out.data_ptr(), LSEK_EP_HANDLE_BYTES));
+  return out;
+}
+
+void ep_domain_import(int64_t h, int64_t peer, torch::Tensor handle) {
+  TORCH_CHECK(!handle.is_cuda() && handle.is_contiguous() && handle.scalar_type() == at::kByte &&
+                  handle.numel() >= LSEK_EP_HANDLE_BYTES,
+              "ep_domain_import: handle must be a CPU uint8 tensor of 64 bytes");
+  check_status(lsek_ep_domain_import(domain_of(h), to_i32(peer, "peer"), handle.data_ptr(),
+                                     static_cast<size_t>(handle.numel())));
+}
+
+// Non-owning views of this rank's buffers: (recv_rows, recv_ids, recv_w, back).
+std::vector<torch::Tensor> ep_domain_buffers(int64_t h, int64_t hidden_dim, int64_t topk) {
+  void *rows = nullptr, *back = nullptr;
+  int32_t* ids = nullptr;
+  float* w = nullptr;
+  int64_t cap_rows = 0, cap_slots = 0;
+  check_status(lsek_ep_domain_buffers(domain_of(h), &rows, &ids, &w, &back, &cap_rows, &cap_slots));
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  auto o = torch::TensorOptions().device(torch::kCUDA, dev);
+  return {torch::from_blob(rows, {cap_rows, hidden_dim}, o.dtype(at::kBFloat16)),
+          torch::from_blob(ids, {cap_rows, topk}, o.dtype(at::kInt)),
+          torch::from_blob(w, {cap_rows, topk}, o.dtype(at::kFloat)),
+          torch::from_blob(back, {cap_slots, hidden_dim}, o.dtype(at::kBFloat16))};
+}
+
+void ep_domain_destroy(int64_t h) {
+  if (h != 0) lsek_ep_domain_destroy(domain_of(h));
+}
+
+torch::Tensor ep_dispatch_push(int64_t h, torch::Tensor counts, torch::Tensor hidden,
+                               torch::Tensor topk_indices, torch::Tensor topk_weights,
+                               torch::Tensor pair_row, torch::Tensor send_off, int64_t rows,
+                               int64_t num_experts, int64_t epoch) {
+  check_counts(counts);
+  TORCH_CHECK(hidden.is_cuda() && hidden.is_contiguous() && hidden.scalar_type() == at::kBFloat16,
+              "ep_dispatch_push: hidden must be a contiguous bf16 CUDA tensor");
+  check_i32_cuda(topk_indices, "ep_dispatch_push: topk_indices");
+  check_i32_cuda(pair_row, "ep_dispatch_push: pair_row");
+  check_i32_cuda(send_off, "ep_dispatch_push: send_off");
+  TORCH_CHECK(topk_weights.is_cuda() && topk_weights.is_contiguous() &&
+                  topk_weights.scalar_type() == at::kFloat,
+              "ep_dispatch_push: topk_weights must be a contiguous float32 CUDA tensor");
+  const c10::cuda::OptionalCUDAGuard guard(hidden.device());
+  const int64_t T = hidden.size(0), k = topk_indices.size(1);
+  auto send_ids = torch::empty({rows, k}, topk_indices.options());
+  check_status(lsek_ep_dispatch_push(
+      domain_of(h), send_ids.data_ptr<int32_t>(), to_i32(rows, "rows"), counts.data_ptr<int32_t>(),
+      hidden.data_ptr(), topk_indices.data_ptr<int32_t>(), topk_weights.data_ptr<float>(),
+      pair_row.data_ptr<int32_t>(), send_off.data_ptr<int32_t>(), to_i32(T, "T"),
+      to_i32(num_experts, "E"), static_cast<uint32_t>(epoch), stream_of(hidden)));
+  return send_ids;
+}
+
+void ep_wait(int64_t h, int64_t what, int64_t epoch, int64_t timeout_ns) {
+  check_status(lsek_ep_wait(domain_of(h), to_i32(what, "what"), static_cast<uint32_t>(epoch),
+                            timeout_ns, at::cuda::getCurrentCUDAStream().stream()));
+}
+
+std::vector<torch::Tensor> ep_combine_plan(int64_t h, torch::Tensor s2d, torch::Tensor slot_row,
+                                           torch::Tensor counts, int64_t recv_rows,
+                                           int64_t valid_slots) {
+  check_counts(counts);
+  check_i32_cuda(s2d, "ep_combine_plan: s2d");
+  check_i32_cuda(slot_row, "ep_combine_plan: slot_row");
+  const c10::cuda::OptionalCUDAGuard guard(s2d.device());
+  auto dst_rank = torch::empty({valid_slots}, s2d.options());
+  auto dst_row = torch::empty({valid_slots}, s2d.options());
+  auto dst_w = torch::empty({valid_slots}, s2d.options().dtype(at::kFloat));
+  check_status(lsek_ep_combine_plan(domain_of(h), dst_rank.data_ptr<int32_t>(),
+                                    dst_row.data_ptr<int32_t>(), dst_w.data_ptr<float>(),
+                                    s2d.data_ptr<int32_t>(), slot_row.data_ptr<int32_t>(),
+                                    counts.data_ptr<int32_t>(), to_i32(recv_rows, "recv_rows"),
+                                    to_i32(valid_slots, "valid_slots"), stream_of(s2d)));
+  return {dst_rank, dst_row, dst_w};
+}
+
+void ep_combine_push(int64_t h, torch::Tensor expert_out, torch::Tensor dst_rank,
+                     torch::Tensor dst_row, torch::Tensor dst_w, int64_t epoch) {
+  TORCH_CHECK(expert_out.is_cuda() && expert_out.is_contiguous() &&
+                  expert_out.scalar_type() == at::kBFloat16,
+              "ep_combine_push: expert_out must be a contiguous bf16 CUDA tensor");
+  check_i32_cuda(dst_rank, "ep_combine_push: dst_rank");
+  check_i32_cuda(dst_row, "ep_combine_push: dst_row");
+  const c10::cuda::OptionalCUDAGuard guard(expert_out.device());
+  TORCH_CHECK(dst_rank.numel() <= expert_out.size(0), "ep_combine_push: more plan rows than outputs");
+  check_status(lsek_ep_combine_push(domain_of(h), expert_out.data_ptr(),
+                                    dst_rank.data_ptr<int32_t>(), dst_row.data_ptr<int32_t>(),
+                                    dst_w.data_ptr<float>(), to_i32(dst_rank.numel(), "rows"),
+                                    static_cast<uint32_t>(epoch), stream_of(expert_out)));
+}
+
+void ep_down_gemm_combine(int64_t h, torch::Tensor hact, torch::Tensor w_down,
+                          torch::Tensor expert_offsets, torch::Tensor dst_rank,
+                          torch::Tensor dst_row, torch::Tensor dst_w, int64_t epoch) {
+  TORCH_CHECK(hact.is_cuda() && hact.is_contiguous() && hact.scalar_type() == at::kBFloat16 &&
+                  hact.dim() == 2,
+              "ep_down_gemm_combine: h must be a contiguous bf16 CUDA tensor [rows, I]");
+  TORCH_CHECK(w_down.is_cuda() && w_down.is_contiguous() && w_down.scalar_type() == at::kBFloat16 &&
+                  w_down.dim() == 3,
+              "ep_down_gemm_combine: W_down must be a contiguous bf16 CUDA tensor [E, H, I]");
+  check_i32_cuda(expert_offsets, "ep_down_gemm_combine: expert_offsets");
+  const c10::cuda::OptionalCUDAGuard guard(hact.device());
+  TORCH_CHECK(dst_rank.numel() >= hact.size(0), "ep_down_gemm_combine: plan shorter than rows");
+  auto ws = torch::empty({LSEK_GEMM_WORKSPACE_BYTES}, hact.options().dtype(at::kByte));
+  check_status(lsek_ep_down_gemm_combine(
+      domain_of(h), hact.data_ptr(), w_down.data_ptr(), expert_offsets.data_ptr<int32_t>(),
+      to_i32(w_down.size(0), "local_experts"), to_i32(hact.size(0), "rows"),
+      to_i32(hact.size(1), "I"), dst_rank.data_ptr<int32_t>(), dst_row.data_ptr<int32_t>(),
+      dst_w.data_ptr<float>(), static_cast<uint32_t>(epoch), ws.data_ptr(), LSEK_GEMM_WORKSPACE_BYTES,
+      stream_of(hact)));
+}
+
 // Timing events for lsek_moe_layer_forward's stage_events: created with
 // timing enabled, recorded by the library on the layer's stream, read back
 // as milliseconds between consecutive events.
@@ -598,6 +737,26 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("weights"), py::arg("slot_row"), py::arg("comb_rows"));
   m.def("ep_combine_reduce", &ep_combine_reduce, py::arg("comb_rows"), py::arg("topk_indices"),
         py::arg("pair_row"), py::arg("slot_row"), py::arg("num_experts"), py::arg("world_size"));
+  m.def("ep_domain_create", &ep_domain_create, py::arg("rank"), py::arg("world_size"),
+        py::arg("max_tokens"), py::arg("hidden_dim"), py::arg("topk"));
+  m.def("ep_domain_export", &ep_domain_export, py::arg("domain"));
+  m.def("ep_domain_import", &ep_domain_import, py::arg("domain"), py::arg("peer"),
+        py::arg("handle"));
+  m.def("ep_domain_buffers", &ep_domain_buffers, py::arg("domain"), py::arg("hidden_dim"),
+        py::arg("topk"));
+  m.def("ep_domain_destroy", &ep_domain_destroy, py::arg("domain"));
+  m.def("ep_dispatch_push", &ep_dispatch_push, py::arg("domain"), py::arg("counts"),
+        py::arg("hidden"), py::arg("topk_indices"), py::arg("topk_weights"), py::arg("pair_row"),
+        py::arg("send_off"), py::arg("rows"), py::arg("num_experts"), py::arg("epoch"));
+  m.def("ep_wait", &ep_wait, py::arg("domain"), py::arg("what"), py::arg("epoch"),
+        py::arg("timeout_ns") = 0);
+  m.def("ep_combine_plan", &ep_combine_plan, py::arg("domain"), py::arg("s2d"),
+        py::arg("slot_row"), py::arg("counts"), py::arg("recv_rows"), py::arg("valid_slots"));
+  m.def("ep_combine_push", &ep_combine_push, py::arg("domain"), py::arg("expert_out"),
+        py::arg("dst_rank"), py::arg("dst_row"), py::arg("dst_w"), py::arg("epoch"));
+  m.def("ep_down_gemm_combine", &ep_down_gemm_combine, py::arg("domain"), py::arg("h"),
+        py::arg("w_down"), py::arg("expert_offsets"), py::arg("dst_rank"), py::arg("dst_row"),
+        py::arg("dst_w"), py::arg("epoch"));
   m.def("events_create", &events_create, py::arg("n"));
   m.def("events_elapsed_ms", &events_elapsed_ms, py::arg("handles"));
   m.def("events_destroy", &events_destroy, py::arg("handles"));

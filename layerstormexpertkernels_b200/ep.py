@@ -123,6 +123,155 @@ class Dispatch:
         return sum(self.recv_slots_n)
 
 
+# ---------------------------------------------------------------------------
+# Peer-memory transport: the kernels move the data over NVLink themselves
+# ---------------------------------------------------------------------------
+
+
+class PeerDomain:
+    """The symmetric buffers of an expert-parallel group on one node.
+
+    Every rank allocates one buffer (liblsek lsek_ep_domain_create), the
+    ranks swap its CUDA IPC handle over the process group once, and the
+    dispatch / combine kernels then store straight into the owner's buffer.
+    `max_tokens` bounds the tokens of one rank per layer call.  close() (or
+    leaving a `with` block) frees the buffers after a barrier, so no peer
+    still writes into them."""
+
+    def __init__(self, max_tokens: int, hidden_dim: int, topk: int, group=None):
+        ex = ProcessGroupExchange(group)
+        self.group, self.world_size, self.rank = group, ex.world_size, ex.rank
+        self.max_tokens, self.hidden_dim, self.topk = max_tokens, hidden_dim, topk
+        self.handle = _C.ep_domain_create(self.rank, self.world_size, max_tokens, hidden_dim, topk)
+        try:
+            if self.world_size > 1:
+                mine = _C.ep_domain_export(self.handle)
+                dev = torch.device("cuda", torch.cuda.current_device())
+                every = torch.empty(self.world_size * mine.numel(), dtype=torch.uint8, device=dev)
+                dist.all_gather_into_tensor(every, mine.to(dev), group=group)
+                every = every.view(self.world_size, -1).cpu()
+                for g in range(self.world_size):
+                    if g != self.rank:
+                        _C.ep_domain_import(self.handle, g, every[g].contiguous())
+                dist.barrier(group=group)
+        except BaseException:
+            _C.ep_domain_destroy(self.handle)
+            self.handle = 0
+            raise
+        (self.recv_rows, self.recv_ids, self.recv_w,
+         self.back) = _C.ep_domain_buffers(self.handle, hidden_dim, topk)
+        self.epoch = 0
+
+    def next_epoch(self) -> int:
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        return self.epoch
+
+    def close(self):
+        if self.handle:
+            torch.cuda.synchronize()
+            if self.world_size > 1:
+                dist.barrier(group=self.group)
+            self.recv_rows = self.recv_ids = self.recv_w = self.back = None
+            _C.ep_domain_destroy(self.handle)
+            self.handle = 0
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+@dataclass
+class PeerDispatch:
+    """One dispatch over a PeerDomain, needed again by the combine."""
+
+    domain: PeerDomain
+    epoch: int
+    counts: torch.Tensor        # [G, G, 2] host: (rows, slots) rank s sends to rank g
+    num_experts: int
+    topk_indices: torch.Tensor
+    pair_row: torch.Tensor
+    send_ids: torch.Tensor
+    recv_rows: torch.Tensor     # views of the domain's receive buffers
+    recv_ids: torch.Tensor
+    recv_w: torch.Tensor
+
+    @property
+    def valid_slots(self) -> int:
+        return int(self.counts[:, self.domain.rank, 1].sum())
+
+    @property
+    def back_rows(self) -> int:
+        return int(self.counts[self.domain.rank, :, 1].sum())
+
+
+def _gather_counts(send_counts: torch.Tensor, domain: PeerDomain) -> torch.Tensor:
+    G = domain.world_size
+    if G == 1:
+        return send_counts.reshape(1, 1, 2).cpu()
+    every = torch.empty(G * G * 2, dtype=torch.int32, device=send_counts.device)
+    dist.all_gather_into_tensor(every, send_counts.reshape(-1), group=domain.group)
+    return every.view(G, G, 2).cpu()
+
+
+def peer_dispatch(domain: PeerDomain, hidden: torch.Tensor, topk_indices: torch.Tensor,
+                  topk_weights: torch.Tensor, num_experts: int, steps=DeviceSteps,
+                  mark: Optional[Callable[[str], None]] = None) -> PeerDispatch:
+    """Plan, then push every token row into its expert ranks' receive
+    buffers and wait (bounded) for every rank's rows."""
+    G, me = domain.world_size, domain.rank
+    send_off, send_counts, pair_row, _ = steps.plan(topk_indices, num_experts, G)
+    counts = _gather_counts(send_counts, domain)
+    if mark:
+        mark("ep_plan")
+    epoch = domain.next_epoch()
+    rows = int(counts[me, :, 0].sum())
+    send_ids = _C.ep_dispatch_push(domain.handle, counts, hidden, topk_indices, topk_weights,
+                                   pair_row, send_off, rows, num_experts, epoch)
+    if mark:
+        mark("ep_dispatch_push")
+    _C.ep_wait(domain.handle, 0, epoch)
+    if mark:
+        mark("ep_dispatch_wait")
+    R = int(counts[:, me, 0].sum())
+    return PeerDispatch(domain, epoch, counts, num_experts, topk_indices, pair_row, send_ids,
+                        domain.recv_rows[:R], domain.recv_ids[:R], domain.recv_w[:R])
+
+
+def peer_combine_plan(pd: PeerDispatch, src_to_dest_map: torch.Tensor, steps=DeviceSteps):
+    """(dst_rank, dst_row, dst_w) of every permuted row of the received slots."""
+    slot_row = steps.slot_scan(pd.recv_ids)
+    return _C.ep_combine_plan(pd.domain.handle, src_to_dest_map, slot_row, pd.counts,
+                              pd.recv_rows.shape[0], pd.valid_slots)
+
+
+def peer_combine_finish(pd: PeerDispatch, steps=DeviceSteps,
+                        mark: Optional[Callable[[str], None]] = None) -> torch.Tensor:
+    """Waits (bounded) for every rank's combine rows, then the fixed-order
+    slot reduce of this rank's tokens."""
+    _C.ep_wait(pd.domain.handle, 1, pd.epoch)
+    if mark:
+        mark("ep_combine_wait")
+    send_slot_row = steps.slot_scan(pd.send_ids)
+    out = steps.combine_reduce(pd.domain.back[:pd.back_rows], pd.topk_indices, pd.pair_row,
+                               send_slot_row, pd.num_experts, pd.domain.world_size)
+    if mark:
+        mark("ep_combine_reduce")
+    return out
+
+
+def peer_combine(pd: PeerDispatch, expert_out: torch.Tensor, src_to_dest_map: torch.Tensor,
+                 steps=DeviceSteps, mark: Optional[Callable[[str], None]] = None) -> torch.Tensor:
+    """The weighted combine of expert outputs already in memory
+    ([valid_slots, H] in the order of src_to_dest_map)."""
+    dst_rank, dst_row, dst_w = peer_combine_plan(pd, src_to_dest_map, steps)
+    _C.ep_combine_push(pd.domain.handle, expert_out, dst_rank, dst_row, dst_w, pd.epoch)
+    if mark:
+        mark("ep_combine_push")
+    return peer_combine_finish(pd, steps, mark)
+
+
 def dispatch(hidden: torch.Tensor, topk_indices: torch.Tensor, topk_weights: torch.Tensor,
              num_experts: int, group=None, steps=DeviceSteps,
              mark: Optional[Callable[[str], None]] = None) -> Dispatch:
@@ -189,13 +338,21 @@ class EPMoELayer:
     `w_gu` [E/G, 2I, H] and `w_down` [E/G, H, I] are the local experts'
     weights (gate rows first, as grouped_gemm_swiglu_bf16 expects); `bias` is
     the full [E] correction bias.  forward(hidden [T, H] bf16, logits [T, E]
-    fp32) returns this rank's [T, H] bf16 layer output."""
+    fp32) returns this rank's [T, H] bf16 layer output.
+
+    With a PeerDomain the exchanges run over peer memory: the dispatch
+    kernel stores rows into the owner ranks and the down-projection GEMM
+    stores each weighted slot into its source rank (the combine fused into
+    the GEMM epilogue).  Without one they are NCCL all-to-alls through
+    `group`."""
 
     def __init__(self, w_gu: torch.Tensor, w_down: torch.Tensor, bias: Optional[torch.Tensor],
                  num_experts: int, topk: int = 8, n_group: int = 8, topk_group: int = 4,
                  routed_scaling_factor: float = 2.5, renormalize: bool = True,
                  scoring_func: str = "sigmoid", swiglu_limit: float = 0.0, group=None,
-                 steps=DeviceSteps):
+                 steps=DeviceSteps, domain: Optional[PeerDomain] = None):
+        if domain is not None:
+            group = domain.group
         group = as_exchange(group)
         world = group.world_size
         if num_experts % world:
@@ -207,7 +364,9 @@ class EPMoELayer:
         self.topk, self.n_group, self.topk_group = topk, n_group, topk_group
         self.routed_scaling_factor, self.renormalize = routed_scaling_factor, renormalize
         self.scoring_func, self.swiglu_limit = scoring_func, swiglu_limit
-        self.group, self.steps = group, steps
+        self.group, self.steps, self.domain = group, steps, domain
+        if domain is not None and domain.world_size != world:
+            raise ValueError("the peer domain and the process group disagree on the world size")
 
     def gate(self, logits: torch.Tensor):
         return self.steps.topk_gating(logits, self.bias, self.topk, self.n_group, self.topk_group,
@@ -232,8 +391,26 @@ class EPMoELayer:
         w, idx = self.gate(logits)
         if mark:
             mark("gating")
+        if self.domain is not None:
+            return self._forward_peer(hidden, idx, w, mark)
         d = dispatch(hidden, idx, w, self.num_experts, self.group, self.steps, mark)
         y, s2d = self.experts(d, mark)
         return combine(d, y, s2d, self.group, self.steps, mark)
+
+    def _forward_peer(self, hidden, idx, w, mark):
+        pd = peer_dispatch(self.domain, hidden, idx, w, self.num_experts, self.steps, mark)
+        permuted, offsets, s2d, _ = self.steps.expert_permute(pd.recv_rows, pd.recv_ids,
+                                                              self.local_experts, pd.valid_slots)
+        if mark:
+            mark("ep_expert_permute")
+        h = self.steps.grouped_gemm_swiglu(permuted, self.w_gu, offsets, self.swiglu_limit)
+        if mark:
+            mark("gate_up_swiglu_gemm")
+        dst_rank, dst_row, dst_w = peer_combine_plan(pd, s2d, self.steps)
+        _C.ep_down_gemm_combine(self.domain.handle, h, self.w_down, offsets, dst_rank, dst_row,
+                                dst_w, pd.epoch)
+        if mark:
+            mark("down_gemm_combine")
+        return peer_combine_finish(pd, self.steps, mark)
 
     __call__ = forward

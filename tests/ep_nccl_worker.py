@@ -1,7 +1,8 @@
 """One rank of the 2-GPU EP parity test (launched by torch.distributed.run
-from tests/test_gpu_ep.py): runs the EP layer over NCCL, then the one-GPU
-canonical path on this rank's tokens with all experts, and writes
-"bit-exact" to <out_dir>/ok<rank> when the two agree."""
+from tests/test_gpu_ep.py): runs the EP layer three times over the chosen
+transport ("nccl": all-to-alls; "peer": peer-memory kernels), then the
+one-GPU canonical path on this rank's tokens with all experts, and writes
+"bit-exact" to <out_dir>/ok<rank> when every call agrees."""
 from __future__ import annotations
 
 import datetime
@@ -17,26 +18,34 @@ for p in (ROOT, os.path.join(ROOT, "tests")):
         sys.path.insert(0, p)
 
 
-def main(out_dir: str) -> int:
+def main(out_dir: str, transport: str) -> int:
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", int(os.environ["LOCAL_RANK"])))
     try:
-        from test_gpu_ep import E_L, K_L, _layer_setup, canonical_gpu
-        from layerstormexpertkernels_b200.ep import EPMoELayer
+        import layerstormexpertkernels_b200 as P
+        from test_gpu_ep import E_L, H_L, K_L, _layer_setup, canonical_gpu
+        from layerstormexpertkernels_b200.ep import EPMoELayer, PeerDomain
 
         tokens = [300 + 57 * r for r in range(world)]
         w_gu, w_down, toks = _layer_setup(world, tokens)
         El = E_L // world
         bias = toks[0].bias.cuda()
+        dom = PeerDomain(max(tokens), H_L, K_L) if transport == "peer" else None
         layer = EPMoELayer(w_gu[rank * El:(rank + 1) * El].contiguous(),
-                           w_down[rank * El:(rank + 1) * El].contiguous(), bias, E_L, topk=K_L)
-        out = layer(toks[rank].hidden.cuda(), toks[rank].logits.cuda())
+                           w_down[rank * El:(rank + 1) * El].contiguous(), bias, E_L, topk=K_L,
+                           domain=dom)
         ref = canonical_gpu(toks[rank], w_gu, w_down, bias)
-        same = torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        same = True
+        for _ in range(3):
+            out = layer(toks[rank].hidden.cuda(), toks[rank].logits.cuda())
+            same &= torch.equal(out.view(torch.int16), ref.view(torch.int16))
         torch.cuda.synchronize()
+        same &= P.device_error() == 0
+        if dom is not None:
+            dom.close()
         with open(os.path.join(out_dir, f"ok{rank}"), "w") as f:
             f.write("bit-exact" if same else "differs")
         dist.barrier()
@@ -46,4 +55,4 @@ def main(out_dir: str) -> int:
 
 
 if __name__ == "__main__":
-    sys.exit(main(sys.argv[1]))
+    sys.exit(main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "nccl"))

@@ -7,7 +7,9 @@
    reference-surface ops (topk_gating, moe_permute, the grouped GEMMs,
    moe_unpermute_bf16_perslot, moe_combine_reduce_slots_bf16_to_bf16):
    identical bits for every G.
-3. The same over NCCL with 2 processes when the box has 2 GPUs."""
+3. The peer-memory path (dispatch pushed into the owner ranks, combine
+   fused into the down-GEMM epilogue) with one rank, its bounded waits, and
+   both transports with 2 processes when the box has 2 GPUs."""
 from __future__ import annotations
 
 import os
@@ -183,14 +185,70 @@ def test_ep_layer_one_rank_process_group_free():
     assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
 
 
-def test_ep_layer_nccl_two_gpus(tmp_path):
-    """Two processes over NCCL (one GPU each), each checking its tokens
-    against the one-GPU canonical path on its own GPU."""
+@pytest.mark.parametrize("tokens", [150, 1])
+def test_ep_layer_peer_domain_one_rank(tokens):
+    """The peer-memory path (push dispatch, combine fused into the down GEMM
+    epilogue) with one rank, over three calls (three epochs)."""
+    from layerstormexpertkernels_b200.ep import EPMoELayer, PeerDomain
+    w_gu, w_down, toks = _layer_setup(1, [tokens])
+    bias = toks[0].bias.cuda()
+    with PeerDomain(max_tokens=512, hidden_dim=H_L, topk=K_L) as dom:
+        layer = EPMoELayer(w_gu, w_down, bias, E_L, topk=K_L, domain=dom)
+        ref = canonical_gpu(toks[0], w_gu, w_down, bias)
+        for _ in range(3):
+            out = layer(toks[0].hidden.cuda(), toks[0].logits.cuda())
+            sync_and_check_device_error()
+            assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        assert dom.epoch == 3
+
+
+def test_peer_combine_push_one_rank():
+    """Dispatch + combine without a GEMM (synthetic expert outputs, as the
+    EP combine benchmark runs it) against the canonical per-slot combine."""
+    import layerstormexpertkernels_b200 as P
+    from layerstormexpertkernels_b200 import ep as EP
+    T, E, H, k = 300, 64, 256, 8
+    idx, w = _routing(T, E, k, seed=5, invalid=False)
+    hidden = MO.bf16_round(np.random.default_rng(1).standard_normal((T, H), dtype=np.float32))
+    with EP.PeerDomain(max_tokens=T, hidden_dim=H, topk=k) as dom:
+        pd = EP.peer_dispatch(dom, bf16_dev(hidden), dev(idx), dev(w), E)
+        permuted, offs, s2d, _ = P._C.ep_expert_permute(pd.recv_rows, pd.recv_ids, E,
+                                                        pd.valid_slots)
+        y = (permuted.float() * 1.5 + 0.25).to(torch.bfloat16)  # a row-wise "expert"
+        out = EP.peer_combine(pd, y, s2d)
+        sync_and_check_device_error()
+    permuted1, offs1, s2d1, _ = P.moe_permute(bf16_dev(hidden), dev(idx), E)
+    y1 = (permuted1.float() * 1.5 + 0.25).to(torch.bfloat16)
+    ref = P.moe_combine_reduce_slots_bf16_to_bf16(
+        P.moe_unpermute_bf16_perslot(y1, dev(w), s2d1, T, k))
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+def test_peer_wait_expires_with_status():
+    """A wait on an epoch nobody publishes gives up after its limit and
+    records kDevErrEpDispatchWait (4); the context stays usable."""
+    import layerstormexpertkernels_b200 as P
+    from layerstormexpertkernels_b200.ep import PeerDomain
+    with PeerDomain(max_tokens=4, hidden_dim=64, topk=2) as dom:
+        P._C.ep_wait(dom.handle, 0, 7, 2_000_000)  # 2 ms
+        assert P.device_error() == 4
+        P._C.ep_wait(dom.handle, 1, 7, 2_000_000)
+        assert P.device_error() == 5
+    x = torch.ones(4, device="cuda")
+    assert float((x + 1).sum()) == 8.0
+    assert P.device_error() == 0
+
+
+@pytest.mark.parametrize("transport", ["nccl", "peer"])
+def test_ep_layer_two_gpus(tmp_path, transport):
+    """Two processes (one GPU each), each checking its tokens against the
+    one-GPU canonical path on its own GPU, over three calls."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
+    port = "29641" if transport == "nccl" else "29643"
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr", "127.0.0.1", "--master-port", "29641",
-           os.path.join(ROOT, "tests", "ep_nccl_worker.py"), str(tmp_path)]
+           "--master-addr", "127.0.0.1", "--master-port", port,
+           os.path.join(ROOT, "tests", "ep_nccl_worker.py"), str(tmp_path), transport]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     res = subprocess.run(["timeout", "-k", "30", "600"] + cmd, cwd=ROOT, env=env,
                          capture_output=True, text=True)
