@@ -446,7 +446,7 @@ def run_ep(args):
     domain = EP.PeerDomain(max(T, CFG3_TOKENS), HIDDEN, TOPK) if peer else None
     layer = EP.EPMoELayer(w_gu, w_down, bias, E, topk=TOPK, n_group=N_GROUP,
                           topk_group=TOPK_GROUP, routed_scaling_factor=RSF, renormalize=True,
-                          domain=domain)
+                          domain=domain, combine=args.combine)
     hidden, logits = x.hidden.to(dev), x.logits.to(dev)
 
     for _ in range(args.warmup):
@@ -514,8 +514,9 @@ def run_ep(args):
 
     plan = 1 + route_launches(T * world) + 1
     permute = route_launches(recv_rows * TOPK) + 1
-    if peer:  # gating, plan, push, wait, permute, gate/up, scan, combine plan, down+combine, wait, scan, reduce
-        launches = 1 + plan + 1 + 1 + permute + 1 + 1 + 1 + 1 + 1 + 1 + 1
+    if peer:  # gating, plan, push, wait, permute, gate/up, scan, combine plan, down(+combine),
+        # [combine push], wait, scan, reduce
+        launches = 1 + plan + 1 + 1 + permute + 1 + 1 + 1 + 1 + (1 if layer.combine == "push" else 0) + 1 + 1 + 1
     else:     # gating, plan, pack, permute, gate/up, down, scan, combine pack, scan, reduce
         launches = 1 + plan + 1 + permute + 2 + 2 + 1 + 1
     if rank == 0:
@@ -523,9 +524,14 @@ def run_ep(args):
         gu_flops = 2.0 * valid * HIDDEN * 2 * INTER
         gu_bytes = El * 2 * INTER * HIDDEN * 2 + valid * HIDDEN * 2 + valid * INTER * 2
         gu_ms = stage_ms["gate_up_swiglu_gemm"]
-        transport = ("peer memory: dispatch kernel stores rows into the owner GPUs, combine "
-                     "fused into the down-GEMM epilogue (NVLink stores), epoch flags"
-                     if peer else "NCCL all-to-all dispatch/combine")
+        if not peer:
+            transport = "NCCL all-to-all dispatch/combine"
+        elif layer.combine == "fused":
+            transport = ("peer memory: dispatch kernel stores rows into the owner GPUs, combine "
+                         "fused into the down-GEMM epilogue (NVLink stores), epoch flags")
+        else:
+            transport = ("peer memory: dispatch kernel stores rows into the owner GPUs, a combine "
+                         "kernel streams the weighted rows back over NVLink, epoch flags")
         achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
         roofline = {"kernel": "gate_up_swiglu_gemm (rank 0)", "bound": "hbm",
                     "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -669,6 +675,9 @@ def main():
                     help="run the expert-parallel arm even on one GPU (default for N > 1)")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="expert-parallel exchange: peer-memory kernels (default) or NCCL all-to-all")
+    ap.add_argument("--combine", choices=["auto", "fused", "push"], default="auto",
+                    help="peer transport: combine fused into the down GEMM, or a separate push "
+                         "kernel (auto: push)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)

@@ -341,16 +341,17 @@ class EPMoELayer:
     fp32) returns this rank's [T, H] bf16 layer output.
 
     With a PeerDomain the exchanges run over peer memory: the dispatch
-    kernel stores rows into the owner ranks and the down-projection GEMM
-    stores each weighted slot into its source rank (the combine fused into
-    the GEMM epilogue).  Without one they are NCCL all-to-alls through
-    `group`."""
+    kernel stores rows into the owner ranks, and the weighted slots go back
+    through a push kernel (combine="push", the default) or straight from the
+    down-projection GEMM's epilogue (combine="fused").  Without a domain
+    they are NCCL all-to-alls through `group`."""
 
     def __init__(self, w_gu: torch.Tensor, w_down: torch.Tensor, bias: Optional[torch.Tensor],
                  num_experts: int, topk: int = 8, n_group: int = 8, topk_group: int = 4,
                  routed_scaling_factor: float = 2.5, renormalize: bool = True,
                  scoring_func: str = "sigmoid", swiglu_limit: float = 0.0, group=None,
-                 steps=DeviceSteps, domain: Optional[PeerDomain] = None):
+                 steps=DeviceSteps, domain: Optional[PeerDomain] = None,
+                 combine: str = "auto"):
         if domain is not None:
             group = domain.group
         group = as_exchange(group)
@@ -367,6 +368,16 @@ class EPMoELayer:
         self.group, self.steps, self.domain = group, steps, domain
         if domain is not None and domain.world_size != world:
             raise ValueError("the peer domain and the process group disagree on the world size")
+        if combine not in ("auto", "fused", "push"):
+            raise ValueError("combine must be 'auto', 'fused' or 'push'")
+        # Peer transport: "fused" stores each weighted slot from the down-GEMM
+        # epilogue straight into its source rank; "push" lets the GEMM write
+        # locally and a row-coalesced kernel stream the rows over NVLink.  The
+        # epilogue's per-thread 64-byte stores to remote memory hold its
+        # accumulator longer, which stalls the GEMM as more rows leave the GPU
+        # (measured on B200: equal at 2 ranks, push 1.3x faster at 8), so
+        # "auto" pushes.
+        self.combine = "push" if combine == "auto" else combine
 
     def gate(self, logits: torch.Tensor):
         return self.steps.topk_gating(logits, self.bias, self.topk, self.n_group, self.topk_group,
@@ -406,6 +417,11 @@ class EPMoELayer:
         h = self.steps.grouped_gemm_swiglu(permuted, self.w_gu, offsets, self.swiglu_limit)
         if mark:
             mark("gate_up_swiglu_gemm")
+        if self.combine == "push":
+            y = self.steps.grouped_gemm(h, self.w_down, offsets)
+            if mark:
+                mark("down_gemm")
+            return peer_combine(pd, y, s2d, self.steps, mark)
         dst_rank, dst_row, dst_w = peer_combine_plan(pd, s2d, self.steps)
         _C.ep_down_gemm_combine(self.domain.handle, h, self.w_down, offsets, dst_rank, dst_row,
                                 dst_w, pd.epoch)

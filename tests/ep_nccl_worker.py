@@ -1,6 +1,8 @@
 """One rank of the 2-GPU EP parity test (launched by torch.distributed.run
 from tests/test_gpu_ep.py): runs the EP layer three times over the chosen
-transport ("nccl": all-to-alls; "peer": peer-memory kernels), then the
+transport ("nccl": all-to-alls; "peer": peer-memory kernels with the combine
+fused into the down GEMM; "peer-push": peer memory with a separate combine
+kernel), then the
 one-GPU canonical path on this rank's tokens with all experts, and writes
 "bit-exact" to <out_dir>/ok<rank> when every call agrees."""
 from __future__ import annotations
@@ -33,10 +35,11 @@ def main(out_dir: str, transport: str) -> int:
         w_gu, w_down, toks = _layer_setup(world, tokens)
         El = E_L // world
         bias = toks[0].bias.cuda()
-        dom = PeerDomain(max(tokens), H_L, K_L) if transport == "peer" else None
+        dom = PeerDomain(max(tokens), H_L, K_L) if transport.startswith("peer") else None
+        combine = "push" if transport == "peer-push" else "fused"
         layer = EPMoELayer(w_gu[rank * El:(rank + 1) * El].contiguous(),
                            w_down[rank * El:(rank + 1) * El].contiguous(), bias, E_L, topk=K_L,
-                           domain=dom)
+                           domain=dom, combine=combine)
         ref = canonical_gpu(toks[rank], w_gu, w_down, bias)
         same = True
         for _ in range(3):

@@ -186,14 +186,16 @@ def test_ep_layer_one_rank_process_group_free():
 
 
 @pytest.mark.parametrize("tokens", [150, 1])
-def test_ep_layer_peer_domain_one_rank(tokens):
-    """The peer-memory path (push dispatch, combine fused into the down GEMM
-    epilogue) with one rank, over three calls (three epochs)."""
+@pytest.mark.parametrize("combine", ["fused", "push"])
+def test_ep_layer_peer_domain_one_rank(tokens, combine):
+    """The peer-memory path (push dispatch; combine fused into the down GEMM
+    epilogue, or a separate push kernel) with one rank, over three calls
+    (three epochs)."""
     from layerstormexpertkernels_b200.ep import EPMoELayer, PeerDomain
     w_gu, w_down, toks = _layer_setup(1, [tokens])
     bias = toks[0].bias.cuda()
     with PeerDomain(max_tokens=512, hidden_dim=H_L, topk=K_L) as dom:
-        layer = EPMoELayer(w_gu, w_down, bias, E_L, topk=K_L, domain=dom)
+        layer = EPMoELayer(w_gu, w_down, bias, E_L, topk=K_L, domain=dom, combine=combine)
         ref = canonical_gpu(toks[0], w_gu, w_down, bias)
         for _ in range(3):
             out = layer(toks[0].hidden.cuda(), toks[0].logits.cuda())
@@ -239,13 +241,13 @@ def test_peer_wait_expires_with_status():
     assert P.device_error() == 0
 
 
-@pytest.mark.parametrize("transport", ["nccl", "peer"])
+@pytest.mark.parametrize("transport", ["nccl", "peer", "peer-push"])
 def test_ep_layer_two_gpus(tmp_path, transport):
     """Two processes (one GPU each), each checking its tokens against the
     one-GPU canonical path on its own GPU, over three calls."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    port = "29641" if transport == "nccl" else "29643"
+    port = {"nccl": "29641", "peer": "29643", "peer-push": "29645"}[transport]
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr", "127.0.0.1", "--master-port", port,
            os.path.join(ROOT, "tests", "ep_nccl_worker.py"), str(tmp_path), transport]
