@@ -355,6 +355,9 @@ def run_ours(args):
             "roofline": roofline,
             "stages": stages,
             "clocks": sampler.summary()}
+    if world == 1 and (T, E) == (T_TOKENS, EXPERTS) and not args.no_sweeps:
+        line["swiglu_sweep"] = swiglu_sweep(peaks)
+        line["decode"] = decode_latency(layer, E, dev, peaks)
     if world == 1 and not args.no_cpu_baseline and (T, E) == (T_TOKENS, EXPERTS):
         import torch as _t
         cores = len(os.sched_getaffinity(0))
@@ -366,6 +369,79 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# SwiGLU sweep and decode latency (N = 1)
+# ---------------------------------------------------------------------------
+
+def _l2_flusher(dev):
+    """Writes 256 MiB (twice the 126 MB L2) so the next kernel starts cold."""
+    import torch
+    buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    return lambda: buf.fill_(1)
+
+
+def swiglu_sweep(peaks, reps=20):
+    """cfg2: fused_swiglu on [N, 2*2048] bf16 ~ N(0,1) -> [N, 2048], N in
+    {256 ... 65536}; 12,288 bytes per row; L2 flushed before every timed call."""
+    import torch
+    import layerstormexpertkernels_b200 as P
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = _l2_flusher(dev)
+    out = {}
+    for n in (256, 1024, 4096, 16384, 65536):
+        g = torch.Generator(device=dev).manual_seed(n)
+        x = torch.randn(n, 2 * INTER, generator=g, device=dev).to(torch.bfloat16)
+        P.fused_swiglu(x)
+        times = []
+        for _ in range(reps):
+            flush()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            P.fused_swiglu(x)
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        gbs = n * 12288 / (ms * 1e-3) / 1e9
+        out[str(n)] = {"us": ms * 1e3, "gbs": gbs, "frac_of_hbm": gbs / peaks["hbm_gbs"]}
+    return {"workload": "cfg2: fused_swiglu [N, 4096] -> [N, 2048] bf16, L2 flushed per call",
+            "by_rows": out}
+
+
+def decode_latency(layer, E, dev, peaks, reps=30):
+    """cfg4: the whole layer at T in {1, 8, 32, 64} with the cfg1 weights
+    resident; floor = bytes of the touched experts' weights / HBM bandwidth."""
+    import torch
+    from layerstormexpertkernels_b200.synthetic import token_inputs
+    out = {}
+    for t in (1, 8, 32, 64):
+        x = token_inputs(t, E, HIDDEN, seed=1000 + t)
+        hidden, logits = x.hidden.to(dev), x.logits.to(dev)
+        y = torch.empty_like(hidden)
+        ti = torch.empty(t, TOPK, dtype=torch.int32, device=dev)
+        tw = torch.empty(t, TOPK, dtype=torch.float32, device=dev)
+        for _ in range(3):
+            layer(hidden, logits, out=y, topk_weights=tw, topk_indices=ti)
+        torch.cuda.synchronize()
+        touched = int(torch.unique(ti).numel())
+        times = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            layer(hidden, logits, out=y)
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        floor_bytes = touched * 3 * INTER * HIDDEN * 2
+        floor_us = floor_bytes / (peaks["hbm_gbs"] * 1e9) * 1e6
+        out[str(t)] = {"us": ms * 1e3, "touched_experts": touched, "floor_us": floor_us,
+                       "frac_of_floor": floor_us / (ms * 1e3)}
+    return {"workload": "cfg4: decode-shaped layer, T in {1, 8, 32, 64}, cfg1 weights resident "
+                        "(22.5 GB, larger than L2, so touched experts stream from HBM)",
+            "by_tokens": out}
 
 
 # ---------------------------------------------------------------------------
@@ -671,6 +747,8 @@ def main():
     ap.add_argument("--experts", type=int, default=EXPERTS,
                     help="routed experts (default 256); smaller values make profiling cases")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweeps", action="store_true",
+                    help="skip the cfg2 SwiGLU sweep and the cfg4 decode latencies")
     ap.add_argument("--ep", action="store_true",
                     help="run the expert-parallel arm even on one GPU (default for N > 1)")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
