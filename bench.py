@@ -358,6 +358,7 @@ def run_ours(args):
     if world == 1 and (T, E) == (T_TOKENS, EXPERTS) and not args.no_sweeps:
         line["swiglu_sweep"] = swiglu_sweep(peaks)
         line["decode"] = decode_latency(layer, E, dev, peaks)
+        line["gemm_compute_sweep"] = gemm_compute_sweep(w_gu, w_down, x.bias.to(dev), E, dev, peaks)
     if world == 1 and not args.no_cpu_baseline and (T, E) == (T_TOKENS, EXPERTS):
         import torch as _t
         cores = len(os.sched_getaffinity(0))
@@ -442,6 +443,51 @@ def decode_latency(layer, E, dev, peaks, reps=30):
     return {"workload": "cfg4: decode-shaped layer, T in {1, 8, 32, 64}, cfg1 weights resident "
                         "(22.5 GB, larger than L2, so touched experts stream from HBM)",
             "by_tokens": out}
+
+
+def gemm_compute_sweep(w_gu, w_down, bias, E, dev, peaks, reps=5):
+    """The expert GEMMs where they are compute-bound: T in {16384, 32768}
+    tokens (512 and 1024 rows per expert on average) on the resident cfg1
+    weights; TFLOP/s against the measured sustained bf16 peak (seconds-long
+    GEMMs run under the power cap)."""
+    import torch
+    import layerstormexpertkernels_b200 as P
+    from layerstormexpertkernels_b200.synthetic import token_inputs
+    out = {}
+    for t in (16384, 32768):
+        x = token_inputs(t, E, HIDDEN, seed=2000 + t)
+        w, idx = P.topk_gating(x.logits.to(dev), bias, TOPK, N_GROUP, TOPK_GROUP, RSF, True)
+        permuted, offs, _, _ = P.moe_permute(x.hidden.to(dev), idx, E)
+        del x
+        rows = permuted.shape[0]
+        res = {}
+        for name, fn, flops in (
+                ("gate_up_swiglu", lambda: P.grouped_gemm_swiglu_bf16(permuted, w_gu, offs),
+                 2.0 * rows * HIDDEN * 2 * INTER),
+                ("down", None, 2.0 * rows * INTER * HIDDEN)):
+            if fn is None:
+                h = P.grouped_gemm_swiglu_bf16(permuted, w_gu, offs)
+                fn = lambda h=h: P.grouped_gemm_bf16(h, w_down, offs)
+            fn()
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(reps):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                fn()
+                b.record()
+                torch.cuda.synchronize()
+                times.append(a.elapsed_time(b))
+            ms = statistics.median(times)
+            tf = flops / (ms * 1e-3) / 1e12
+            res[name] = {"ms": ms, "tflops": tf,
+                         "frac_of_sustained": tf / peaks["bf16_tflops_sustained"],
+                         "frac_of_burst": tf / peaks["bf16_tflops"]}
+        del permuted
+        torch.cuda.empty_cache()
+        out[str(t)] = res
+    return {"workload": "expert GEMMs at T in {16384, 32768} tokens (E=256, top-8, cfg1 weights): "
+                        "compute-bound", "by_tokens": out}
 
 
 # ---------------------------------------------------------------------------

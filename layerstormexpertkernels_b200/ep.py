@@ -55,6 +55,9 @@ class DeviceSteps:
     topk_gating = staticmethod(_C.topk_gating)
     grouped_gemm_swiglu = staticmethod(_C.grouped_gemm_swiglu_bf16)
     grouped_gemm = staticmethod(_C.grouped_gemm_bf16)
+    moe_permute = staticmethod(_C.moe_permute)
+    unpermute_perslot = staticmethod(_C.moe_unpermute_bf16_perslot)
+    reduce_slots = staticmethod(_C.moe_combine_reduce_slots_bf16_to_bf16)
 
 
 def _as_words(t: torch.Tensor) -> torch.Tensor:
@@ -85,6 +88,20 @@ class ProcessGroupExchange:
         dist.all_to_all_single(_as_words(recv), _as_words(send), output_split_sizes=recv_splits,
                                input_split_sizes=send_splits, group=self.group)
         return recv
+
+    def all_reduce_sum(self, t: torch.Tensor) -> torch.Tensor:
+        """In-place SUM over the ranks.  bf16 reduces natively on GPUs; on
+        the CPU (gloo) it goes through fp32, which is exact for the sums of
+        one value and zeros this module uses it for."""
+        if self.world_size == 1:
+            return t
+        if t.is_cuda or t.dtype != torch.bfloat16:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+            return t
+        f = t.float()
+        dist.all_reduce(f, op=dist.ReduceOp.SUM, group=self.group)
+        t.copy_(f)
+        return t
 
 
 def as_exchange(group):
@@ -430,3 +447,41 @@ class EPMoELayer:
         return peer_combine_finish(pd, self.steps, mark)
 
     __call__ = forward
+
+
+def replicated_forward(hidden: torch.Tensor, logits: torch.Tensor, bias: Optional[torch.Tensor],
+                       w_gu: torch.Tensor, w_down: torch.Tensor, num_experts: int,
+                       topk: int = 8, n_group: int = 8, topk_group: int = 4,
+                       routed_scaling_factor: float = 2.5, renormalize: bool = True,
+                       scoring_func: str = "sigmoid", swiglu_limit: float = 0.0, group=None,
+                       steps=DeviceSteps) -> torch.Tensor:
+    """The reference consumer's expert-parallel contract
+    (smxx/permute/moe_permute.h:67-99; tests/test_kernels.py:131-142,
+    187-200): every rank holds the same tokens and the experts are sharded
+    (rank r owns experts [r*E/G, (r+1)*E/G), `w_gu` / `w_down` hold those).
+    Each rank computes the per-slot rows bf16(w * y) of its own experts, zero
+    for the other slots; a bf16 SUM all-reduce of the [T, topk, H] rows
+    leaves every slot with its one non-zero contribution, and the fixed-order
+    slot reduce gives [T, H].  Exact: a sum of one value and zeros is that
+    value, so every rank returns the one-GPU canonical result bit for bit.
+    Moves T*topk*H*2 bytes per rank through the all-reduce where the
+    dispatch/combine path (EPMoELayer) moves only the rows that change rank.
+    """
+    ex = as_exchange(group)
+    G, r = ex.world_size, ex.rank
+    if num_experts % G:
+        raise ValueError(f"num_experts={num_experts} is not a multiple of world size {G}")
+    El = num_experts // G
+    T = hidden.shape[0]
+    w, idx = steps.topk_gating(logits, bias, topk, n_group, topk_group, routed_scaling_factor,
+                               renormalize, scoring_func)
+    permuted, offsets, s2d, _ = steps.moe_permute(hidden, idx, num_experts)
+    local = offsets[r * El:(r + 1) * El + 1]
+    h = steps.grouped_gemm_swiglu(permuted, w_gu, local, swiglu_limit)
+    y = steps.grouped_gemm(h, w_down, local)
+    lo, hi = (int(v) for v in local[[0, -1]].tolist())
+    y[:lo].zero_()
+    y[hi:].zero_()
+    perslot = steps.unpermute_perslot(y, w, s2d, T, topk)
+    ex.all_reduce_sum(perslot)
+    return steps.reduce_slots(perslot)

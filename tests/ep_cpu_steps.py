@@ -75,6 +75,20 @@ class CpuSteps:
     def grouped_gemm(a, b, offsets):
         return _bf16(MO.grouped_gemm(_np(a), _np(b), _np(offsets)).astype(np.float32))
 
+    @staticmethod
+    def moe_permute(hidden, topk_indices, num_experts):
+        p, off, s2d, perm = MO.moe_permute(_np(hidden), _np(topk_indices), num_experts)
+        return _bf16(p), _i32(off), _i32(s2d), _i32(perm)
+
+    @staticmethod
+    def unpermute_perslot(y, topk_weights, s2d, num_tokens, topk):
+        return _bf16(MO.moe_unpermute_perslot_bf16(_np(y), _np(topk_weights), _np(s2d), num_tokens,
+                                                   topk))
+
+    @staticmethod
+    def reduce_slots(perslot):
+        return _bf16(MO.reduce_slots(_np(perslot)))
+
 
 def canonical_layer(hidden, logits, bias, w_gu, w_down, topk=8, n_group=8, topk_group=4,
                     scale=2.5, renormalize=True):

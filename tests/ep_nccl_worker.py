@@ -2,7 +2,8 @@
 from tests/test_gpu_ep.py): runs the EP layer three times over the chosen
 transport ("nccl": all-to-alls; "peer": peer-memory kernels with the combine
 fused into the down GEMM; "peer-push": peer memory with a separate combine
-kernel), then the
+kernel; "replicated": every rank holds the same tokens and the per-slot
+rows are SUM all-reduced), then the
 one-GPU canonical path on this rank's tokens with all experts, and writes
 "bit-exact" to <out_dir>/ok<rank> when every call agrees."""
 from __future__ import annotations
@@ -40,10 +41,19 @@ def main(out_dir: str, transport: str) -> int:
         layer = EPMoELayer(w_gu[rank * El:(rank + 1) * El].contiguous(),
                            w_down[rank * El:(rank + 1) * El].contiguous(), bias, E_L, topk=K_L,
                            domain=dom, combine=combine)
-        ref = canonical_gpu(toks[rank], w_gu, w_down, bias)
+        if transport == "replicated":  # every rank holds rank 0's tokens
+            from layerstormexpertkernels_b200.ep import replicated_forward
+            ref = canonical_gpu(toks[0], w_gu, w_down, bias)
+            run = lambda: replicated_forward(
+                toks[0].hidden.cuda(), toks[0].logits.cuda(), bias,
+                w_gu[rank * El:(rank + 1) * El].contiguous(),
+                w_down[rank * El:(rank + 1) * El].contiguous(), E_L, topk=K_L)
+        else:
+            ref = canonical_gpu(toks[rank], w_gu, w_down, bias)
+            run = lambda: layer(toks[rank].hidden.cuda(), toks[rank].logits.cuda())
         same = True
         for _ in range(3):
-            out = layer(toks[rank].hidden.cuda(), toks[rank].logits.cuda())
+            out = run()
             same &= torch.equal(out.view(torch.int16), ref.view(torch.int16))
         torch.cuda.synchronize()
         same &= P.device_error() == 0

@@ -200,3 +200,62 @@ def test_ep_layer_loopback_threads(G):
         ref = canonical_layer(hidden, logits, bias, w_gu, w_down, topk=K_G, n_group=4,
                               topk_group=2)
         assert np.array_equal(outs[r].float().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+def _replicated_worker(rank, world, port, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from ep_cpu_steps import CpuSteps
+        from layerstormexpertkernels_b200.ep import replicated_forward
+
+        w_gu, w_down, bias, toks = _layer_inputs()
+        El = E_G // world
+        sl = slice(rank * El, (rank + 1) * El)
+        hidden, logits = toks[0]  # every rank holds the same tokens
+        out = replicated_forward(torch.from_numpy(hidden).to(torch.bfloat16),
+                                 torch.from_numpy(logits), torch.from_numpy(bias),
+                                 torch.from_numpy(w_gu[sl]).to(torch.bfloat16),
+                                 torch.from_numpy(w_down[sl]).to(torch.bfloat16), E_G, topk=K_G,
+                                 n_group=4, topk_group=2, steps=CpuSteps)
+        np.save(os.path.join(out_dir, f"rep{rank}.npy"), out.float().numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_replicated_mode_gloo_world2(tmp_path):
+    """The reference consumer's contract (replicated tokens, bf16 SUM
+    all-reduce of the per-slot rows) gives the one-rank bits on every rank."""
+    mp.spawn(_replicated_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    from ep_cpu_steps import canonical_layer
+    w_gu, w_down, bias, toks = _layer_inputs()
+    hidden, logits = toks[0]
+    ref = canonical_layer(hidden, logits, bias, w_gu, w_down, topk=K_G, n_group=4, topk_group=2)
+    for r in range(2):
+        got = np.load(tmp_path / f"rep{r}.npy")
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("G", [1, 4])
+def test_replicated_mode_loopback_threads(G):
+    from ep_cpu_steps import CpuSteps, canonical_layer
+    from ep_loopback import LoopbackHub
+    from layerstormexpertkernels_b200.ep import replicated_forward
+
+    w_gu, w_down, bias, toks = _layer_inputs()
+    hidden, logits = toks[1]
+    El = E_G // G
+
+    def rank_fn(r, ex):
+        sl = slice(r * El, (r + 1) * El)
+        return replicated_forward(torch.from_numpy(hidden).to(torch.bfloat16),
+                                  torch.from_numpy(logits), torch.from_numpy(bias),
+                                  torch.from_numpy(w_gu[sl]).to(torch.bfloat16),
+                                  torch.from_numpy(w_down[sl]).to(torch.bfloat16), E_G, topk=K_G,
+                                  n_group=4, topk_group=2, group=ex, steps=CpuSteps)
+
+    outs = LoopbackHub(G).run(rank_fn)
+    ref = canonical_layer(hidden, logits, bias, w_gu, w_down, topk=K_G, n_group=4, topk_group=2)
+    for r in range(G):
+        assert np.array_equal(outs[r].float().numpy().view(np.uint32), ref.view(np.uint32))

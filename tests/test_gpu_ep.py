@@ -174,6 +174,30 @@ def test_ep_layer_threads_bit_exact(G, tokens):
         assert stages[r][0] == "gating" and stages[r][-1] == "ep_combine_reduce"
 
 
+@pytest.mark.parametrize("G", [2, 4])
+def test_replicated_mode_threads_bit_exact(G):
+    """The reference consumer's contract: replicated tokens, local experts'
+    per-slot rows, SUM all-reduce (in-process here), fixed-order reduce."""
+    from ep_loopback import LoopbackHub
+    from layerstormexpertkernels_b200.ep import replicated_forward
+
+    w_gu, w_down, toks = _layer_setup(1, [333])
+    bias = toks[0].bias.cuda()
+    El = E_L // G
+
+    def rank_fn(r, ex):
+        return replicated_forward(toks[0].hidden.cuda(), toks[0].logits.cuda(), bias,
+                                  w_gu[r * El:(r + 1) * El].contiguous(),
+                                  w_down[r * El:(r + 1) * El].contiguous(), E_L, topk=K_L,
+                                  group=ex)
+
+    outs = LoopbackHub(G).run(rank_fn)
+    sync_and_check_device_error()
+    ref = canonical_gpu(toks[0], w_gu, w_down, bias)
+    for r in range(G):
+        assert torch.equal(outs[r].view(torch.int16), ref.view(torch.int16)), f"rank {r}"
+
+
 def test_ep_layer_one_rank_process_group_free():
     """No process group: ProcessGroupExchange is a single rank."""
     from layerstormexpertkernels_b200.ep import EPMoELayer
@@ -241,13 +265,13 @@ def test_peer_wait_expires_with_status():
     assert P.device_error() == 0
 
 
-@pytest.mark.parametrize("transport", ["nccl", "peer", "peer-push"])
+@pytest.mark.parametrize("transport", ["nccl", "peer", "peer-push", "replicated"])
 def test_ep_layer_two_gpus(tmp_path, transport):
     """Two processes (one GPU each), each checking its tokens against the
     one-GPU canonical path on its own GPU, over three calls."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    port = {"nccl": "29641", "peer": "29643", "peer-push": "29645"}[transport]
+    port = {"nccl": "29641", "peer": "29643", "peer-push": "29645", "replicated": "29647"}[transport]
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr", "127.0.0.1", "--master-port", port,
            os.path.join(ROOT, "tests", "ep_nccl_worker.py"), str(tmp_path), transport]
