@@ -53,6 +53,7 @@ class StageEvents:
     between its stages; elapsed_ms() gives the per-stage milliseconds."""
 
     def __init__(self):
+        self._destroy = _C.events_destroy  # still callable while the interpreter shuts down
         self.handles = _C.events_create(len(STAGES) + 1)
 
     def elapsed_ms(self) -> dict:
@@ -60,7 +61,7 @@ class StageEvents:
 
     def __del__(self):
         if getattr(self, "handles", None):
-            _C.events_destroy(self.handles)
+            self._destroy(self.handles)
             self.handles = []
 
 
