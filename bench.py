@@ -568,7 +568,7 @@ def run_ep(args):
     domain = EP.PeerDomain(max(T, CFG3_TOKENS), HIDDEN, TOPK) if peer else None
     layer = EP.EPMoELayer(w_gu, w_down, bias, E, topk=TOPK, n_group=N_GROUP,
                           topk_group=TOPK_GROUP, routed_scaling_factor=RSF, renormalize=True,
-                          domain=domain, combine=args.combine)
+                          domain=domain, combine=args.combine, push_chunks=args.push_chunks)
     hidden, logits = x.hidden.to(dev), x.logits.to(dev)
 
     for _ in range(args.warmup):
@@ -636,9 +636,10 @@ def run_ep(args):
 
     plan = 1 + route_launches(T * world) + 1
     permute = route_launches(recv_rows * TOPK) + 1
-    if peer:  # gating, plan, push, wait, permute, gate/up, scan, combine plan, down(+combine),
-        # [combine push], wait, scan, reduce
-        launches = 1 + plan + 1 + 1 + permute + 1 + 1 + 1 + 1 + (1 if layer.combine == "push" else 0) + 1 + 1 + 1
+    if peer:  # gating, plan, push, wait, permute, gate/up, scan, combine plan,
+        # down+combine (fused) or push_chunks x (down GEMM, combine push), wait, scan, reduce
+        down = 2 * layer.push_chunks if layer.combine == "push" else 1
+        launches = 1 + plan + 1 + 1 + permute + 1 + 1 + 1 + down + 1 + 1 + 1
     else:     # gating, plan, pack, permute, gate/up, down, scan, combine pack, scan, reduce
         launches = 1 + plan + 1 + permute + 2 + 2 + 1 + 1
     if rank == 0:
@@ -802,6 +803,8 @@ def main():
     ap.add_argument("--combine", choices=["auto", "fused", "push"], default="auto",
                     help="peer transport: combine fused into the down GEMM, or a separate push "
                          "kernel (auto: push)")
+    ap.add_argument("--push-chunks", type=int, default=2,
+                    help="push combine: expert groups whose rows stream while the next computes")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)

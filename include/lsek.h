@@ -382,10 +382,15 @@ LSEK_API lsek_status lsek_ep_combine_plan(lsek_ep_domain* d, int32_t* dst_rank, 
                                  int32_t recv_rows, int32_t valid_slots, void* stream);
 /* The combine of expert outputs already in memory (no GEMM in front):
  * bf16(dst_w[p] * expert_out[p]) to row dst_row[p] of rank dst_rank[p]'s
- * combine buffer for p < rows, then publishes combine epoch `epoch`. */
+ * combine buffer for p < rows (or for *row_lo <= p < *row_hi when both
+ * device pointers are given, e.g. two entries of the expert offsets, so the
+ * rows of some experts can go while the GEMM computes the others); then,
+ * if `publish`, publishes combine epoch `epoch` (the last of a series of
+ * calls publishes once every row has been stored). */
 LSEK_API lsek_status lsek_ep_combine_push(lsek_ep_domain* d, const void* expert_out,
                                  const int32_t* dst_rank, const int32_t* dst_row,
-                                 const float* dst_w, int32_t rows, uint32_t epoch,
+                                 const float* dst_w, int32_t rows, const int32_t* row_lo,
+                                 const int32_t* row_hi, int32_t publish, uint32_t epoch,
                                  void* stream);
 /* Down-projection GEMM with the combine fused into its epilogue: for each
  * permuted row p, bf16(dst_w[p] * bf16(H[p] . W_down[e]^T)) goes to row

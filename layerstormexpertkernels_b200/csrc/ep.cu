@@ -378,10 +378,13 @@ __global__ void ep_combine_plan_kernel(int32_t* __restrict__ dst_rank, int32_t* 
 __global__ void __launch_bounds__(kThreads) ep_combine_push_kernel(
     const __grid_constant__ PeerTable peers, size_t back_off, const __nv_bfloat16* __restrict__ y,
     const int32_t* __restrict__ dst_rank, const int32_t* __restrict__ dst_row,
-    const float* __restrict__ dst_w, int32_t rows, int64_t cap_slots, int H, int world, int me,
+    const float* __restrict__ dst_w, int32_t rows, const int32_t* __restrict__ row_lo,
+    const int32_t* __restrict__ row_hi, int publish, int64_t cap_slots, int H, int world, int me,
     uint32_t* done, uint32_t epoch) {
   const int nvec = H / 8;
-  for (int32_t p = blockIdx.x; p < rows; p += gridDim.x) {
+  const int32_t p0 = row_lo ? max(__ldg(row_lo), 0) : 0;
+  const int32_t p1 = row_hi ? min(__ldg(row_hi), rows) : rows;
+  for (int32_t p = p0 + blockIdx.x; p < p1; p += gridDim.x) {
     const int32_t rk = __ldg(dst_rank + p);
     const int32_t dr = __ldg(dst_row + p);
     if (rk < 0 || rk >= world || dr < 0 || dr >= cap_slots) continue;
@@ -399,7 +402,8 @@ __global__ void __launch_bounds__(kThreads) ep_combine_push_kernel(
       *reinterpret_cast<uint4*>(dst + v * 8) = out;
     }
   }
-  grid_release_to_peers(peers, world, me, kCtrlCombineFlags, done, epoch);
+  if (publish) grid_release_to_peers(peers, world, me, kCtrlCombineFlags, done, epoch);
+  else __threadfence_system();  // ordered before the publishing call that follows on the stream
 }
 
 }  // namespace
@@ -776,21 +780,24 @@ extern "C" lsek_status lsek_ep_combine_plan(lsek_ep_domain* h, int32_t* dst_rank
 
 extern "C" lsek_status lsek_ep_combine_push(lsek_ep_domain* h, const void* expert_out,
                                             const int32_t* dst_rank, const int32_t* dst_row,
-                                            const float* dst_w, int32_t rows, uint32_t epoch,
-                                            void* stream) {
+                                            const float* dst_w, int32_t rows,
+                                            const int32_t* row_lo, const int32_t* row_hi,
+                                            int32_t publish, uint32_t epoch, void* stream) {
   lsek_status s = domain_check(h, "ep_combine_push");
   if (s != LSEK_OK) return s;
   const EpDomain& d = h->d;
   LSEK_REQUIRE(rows >= 0, "ep_combine_push: bad row count");
   LSEK_REQUIRE(rows == 0 || (expert_out && dst_rank && dst_row && dst_w),
                "ep_combine_push: NULL tensor pointer");
+  LSEK_REQUIRE((row_lo == nullptr) == (row_hi == nullptr), "ep_combine_push: give both row bounds or none");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint32_t* done = reinterpret_cast<uint32_t*>(d.local + kCtrlGemmDone);
-  LSEK_CUDA_TRY(cudaMemsetAsync(done, 0, sizeof(uint32_t), st));
+  if (publish) LSEK_CUDA_TRY(cudaMemsetAsync(done, 0, sizeof(uint32_t), st));
   const int64_t want = 4ll * num_sms();
   const unsigned grid = static_cast<unsigned>(rows == 0 ? 1 : (rows < want ? rows : want));
   ep_combine_push_kernel<<<grid, kThreads, 0, st>>>(
       peer_table(d), d.lay.back, static_cast<const __nv_bfloat16*>(expert_out), dst_rank, dst_row,
-      dst_w, rows, d.lay.cap_slots, static_cast<int>(d.H), d.world, d.rank, done, epoch);
+      dst_w, rows, row_lo, row_hi, publish, d.lay.cap_slots, static_cast<int>(d.H), d.world, d.rank,
+      done, epoch);
   return check_launch("ep_combine_push");
 }

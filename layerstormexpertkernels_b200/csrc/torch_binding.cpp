@@ -268,6 +268,23 @@ void check_gemm_args(const char* op, const torch::Tensor& A, const torch::Tensor
   TORCH_CHECK(offsets.numel() == W.size(0) + 1, op, ": expert_offsets must hold E+1 entries");
 }
 
+// Writes D[rows of the experts in expert_offsets]; other rows of D are left
+// as they are, so experts can be computed in chunks into one buffer.
+void grouped_gemm_bf16_out(torch::Tensor D, torch::Tensor A, torch::Tensor B,
+                           torch::Tensor expert_offsets) {
+  check_gemm_args("grouped_gemm_bf16_out", A, B, expert_offsets);
+  TORCH_CHECK(D.is_cuda() && D.is_contiguous() && D.scalar_type() == at::kBFloat16 &&
+                  D.dim() == 2 && D.size(0) == A.size(0) && D.size(1) == B.size(1),
+              "grouped_gemm_bf16_out: D must be a contiguous bf16 CUDA tensor [rows, N]");
+  const c10::cuda::OptionalCUDAGuard guard(A.device());
+  auto ws = torch::empty({LSEK_GEMM_WORKSPACE_BYTES}, A.options().dtype(at::kByte));
+  check_status(lsek_grouped_gemm_bf16(D.data_ptr(), A.data_ptr(), B.data_ptr(),
+                                      expert_offsets.data_ptr<int32_t>(), to_i32(B.size(0), "E"),
+                                      to_i32(A.size(0), "rows"), to_i32(B.size(1), "N"),
+                                      to_i32(A.size(1), "K"), ws.data_ptr(),
+                                      LSEK_GEMM_WORKSPACE_BYTES, stream_of(A)));
+}
+
 torch::Tensor grouped_gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor expert_offsets) {
   check_gemm_args("grouped_gemm_bf16", A, B, expert_offsets);
   const c10::cuda::OptionalCUDAGuard guard(A.device());
@@ -605,7 +622,9 @@ std::vector<torch::Tensor> ep_combine_plan(int64_t h, torch::Tensor s2d, torch::
 }
 
 void ep_combine_push(int64_t h, torch::Tensor expert_out, torch::Tensor dst_rank,
-                     torch::Tensor dst_row, torch::Tensor dst_w, int64_t epoch) {
+                     torch::Tensor dst_row, torch::Tensor dst_w, int64_t epoch,
+                     c10::optional<torch::Tensor> row_lo, c10::optional<torch::Tensor> row_hi,
+                     bool publish) {
   TORCH_CHECK(expert_out.is_cuda() && expert_out.is_contiguous() &&
                   expert_out.scalar_type() == at::kBFloat16,
               "ep_combine_push: expert_out must be a contiguous bf16 CUDA tensor");
@@ -613,10 +632,20 @@ void ep_combine_push(int64_t h, torch::Tensor expert_out, torch::Tensor dst_rank
   check_i32_cuda(dst_row, "ep_combine_push: dst_row");
   const c10::cuda::OptionalCUDAGuard guard(expert_out.device());
   TORCH_CHECK(dst_rank.numel() <= expert_out.size(0), "ep_combine_push: more plan rows than outputs");
+  TORCH_CHECK(row_lo.has_value() == row_hi.has_value(), "ep_combine_push: give both row bounds or none");
+  const int32_t* lo = nullptr;
+  const int32_t* hi = nullptr;
+  if (row_lo.has_value()) {
+    check_i32_cuda(*row_lo, "ep_combine_push: row_lo");
+    check_i32_cuda(*row_hi, "ep_combine_push: row_hi");
+    lo = row_lo->data_ptr<int32_t>();
+    hi = row_hi->data_ptr<int32_t>();
+  }
   check_status(lsek_ep_combine_push(domain_of(h), expert_out.data_ptr(),
                                     dst_rank.data_ptr<int32_t>(), dst_row.data_ptr<int32_t>(),
-                                    dst_w.data_ptr<float>(), to_i32(dst_rank.numel(), "rows"),
-                                    static_cast<uint32_t>(epoch), stream_of(expert_out)));
+                                    dst_w.data_ptr<float>(), to_i32(dst_rank.numel(), "rows"), lo,
+                                    hi, publish ? 1 : 0, static_cast<uint32_t>(epoch),
+                                    stream_of(expert_out)));
 }
 
 void ep_down_gemm_combine(int64_t h, torch::Tensor hact, torch::Tensor w_down,
@@ -753,7 +782,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_combine_plan", &ep_combine_plan, py::arg("domain"), py::arg("s2d"),
         py::arg("slot_row"), py::arg("counts"), py::arg("recv_rows"), py::arg("valid_slots"));
   m.def("ep_combine_push", &ep_combine_push, py::arg("domain"), py::arg("expert_out"),
-        py::arg("dst_rank"), py::arg("dst_row"), py::arg("dst_w"), py::arg("epoch"));
+        py::arg("dst_rank"), py::arg("dst_row"), py::arg("dst_w"), py::arg("epoch"),
+        py::arg("row_lo") = py::none(), py::arg("row_hi") = py::none(), py::arg("publish") = true);
+  m.def("grouped_gemm_bf16_out", &grouped_gemm_bf16_out, py::arg("D"), py::arg("A"), py::arg("B"),
+        py::arg("expert_offsets"));
   m.def("ep_down_gemm_combine", &ep_down_gemm_combine, py::arg("domain"), py::arg("h"),
         py::arg("w_down"), py::arg("expert_offsets"), py::arg("dst_rank"), py::arg("dst_row"),
         py::arg("dst_w"), py::arg("epoch"));

@@ -368,7 +368,7 @@ class EPMoELayer:
                  routed_scaling_factor: float = 2.5, renormalize: bool = True,
                  scoring_func: str = "sigmoid", swiglu_limit: float = 0.0, group=None,
                  steps=DeviceSteps, domain: Optional[PeerDomain] = None,
-                 combine: str = "auto"):
+                 combine: str = "auto", push_chunks: int = 2):
         if domain is not None:
             group = domain.group
         group = as_exchange(group)
@@ -395,6 +395,10 @@ class EPMoELayer:
         # (measured on B200: equal at 2 ranks, push 1.3x faster at 8), so
         # "auto" pushes.
         self.combine = "push" if combine == "auto" else combine
+        # "push" computes the down projection in `push_chunks` groups of
+        # experts and streams each group's rows while the next one computes.
+        self.push_chunks = max(1, min(push_chunks, self.local_experts))
+        self._comm_stream = None
 
     def gate(self, logits: torch.Tensor):
         return self.steps.topk_gating(logits, self.bias, self.topk, self.n_group, self.topk_group,
@@ -435,15 +439,39 @@ class EPMoELayer:
         if mark:
             mark("gate_up_swiglu_gemm")
         if self.combine == "push":
-            y = self.steps.grouped_gemm(h, self.w_down, offsets)
-            if mark:
-                mark("down_gemm")
-            return peer_combine(pd, y, s2d, self.steps, mark)
+            return self._down_and_push(pd, h, offsets, s2d, mark)
         dst_rank, dst_row, dst_w = peer_combine_plan(pd, s2d, self.steps)
         _C.ep_down_gemm_combine(self.domain.handle, h, self.w_down, offsets, dst_rank, dst_row,
                                 dst_w, pd.epoch)
         if mark:
             mark("down_gemm_combine")
+        return peer_combine_finish(pd, self.steps, mark)
+
+    def _down_and_push(self, pd, h, offsets, s2d, mark):
+        """Down projection in groups of experts; each group's weighted rows
+        go to their source ranks on a second stream while the next group
+        computes, and the last push publishes the combine epoch."""
+        dst_rank, dst_row, dst_w = peer_combine_plan(pd, s2d, self.steps)
+        y = torch.empty(h.shape[0], self.w_down.shape[1], dtype=h.dtype, device=h.device)
+        main = torch.cuda.current_stream()
+        if self._comm_stream is None:
+            self._comm_stream = torch.cuda.Stream(device=h.device)
+        comm = self._comm_stream
+        El, C = self.local_experts, self.push_chunks
+        bounds = [(c * El) // C for c in range(C + 1)]
+        for c in range(C):
+            lo, hi = bounds[c], bounds[c + 1]
+            _C.grouped_gemm_bf16_out(y, h, self.w_down[lo:hi], offsets[lo:hi + 1])
+            ready = torch.cuda.Event()
+            ready.record(main)
+            comm.wait_event(ready)
+            with torch.cuda.stream(comm):
+                _C.ep_combine_push(pd.domain.handle, y, dst_rank, dst_row, dst_w, pd.epoch,
+                                   row_lo=offsets[lo:lo + 1], row_hi=offsets[hi:hi + 1],
+                                   publish=c == C - 1)
+        main.wait_stream(comm)
+        if mark:
+            mark("down_gemm_push")
         return peer_combine_finish(pd, self.steps, mark)
 
     __call__ = forward
