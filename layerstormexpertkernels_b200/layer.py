@@ -122,3 +122,57 @@ class MoELayer:
         return out
 
     __call__ = forward
+
+
+class HostPipeline:
+    """Feeds a layer from pinned host memory with the copies overlapped.
+
+    `forward(hidden, logits)` runs on the current stream and returns the
+    layer output (a device tensor).  submit() copies one batch from host to
+    device on its own stream into one of `depth` device buffer sets, runs
+    the layer once the copy has landed, and copies the output back to
+    `out_host` on a third stream once the layer is done: while batch i
+    computes, batch i+1 is being copied in and batch i-1 out.  Host buffers
+    must be pinned; `out_host` holds its result after synchronize(), and an
+    input host buffer can be refilled once the stream of the next submit()
+    has copied it (after synchronize(), at the latest).
+    """
+
+    def __init__(self, forward, hidden_shape, logits_shape, device,
+                 hidden_dtype=torch.bfloat16, logits_dtype=torch.float32, depth: int = 2):
+        self.forward = forward
+        self.depth = depth
+        self.hidden = [torch.empty(hidden_shape, dtype=hidden_dtype, device=device)
+                       for _ in range(depth)]
+        self.logits = [torch.empty(logits_shape, dtype=logits_dtype, device=device)
+                       for _ in range(depth)]
+        self.h2d = torch.cuda.Stream(device=device)
+        self.d2h = torch.cuda.Stream(device=device)
+        self.copied_in = [torch.cuda.Event() for _ in range(depth)]
+        self.computed = [torch.cuda.Event() for _ in range(depth)]
+        self.used = [False] * depth
+        self.count = 0
+
+    def submit(self, hidden_host: torch.Tensor, logits_host: torch.Tensor,
+               out_host: torch.Tensor) -> None:
+        s = self.count % self.depth
+        self.count += 1
+        main = torch.cuda.current_stream()
+        if self.used[s]:  # the layer that last read this buffer set has finished
+            self.h2d.wait_event(self.computed[s])
+        with torch.cuda.stream(self.h2d):
+            self.hidden[s].copy_(hidden_host, non_blocking=True)
+            self.logits[s].copy_(logits_host, non_blocking=True)
+            self.copied_in[s].record(self.h2d)
+        main.wait_event(self.copied_in[s])
+        y = self.forward(self.hidden[s], self.logits[s])
+        self.computed[s].record(main)
+        self.used[s] = True
+        self.d2h.wait_event(self.computed[s])
+        with torch.cuda.stream(self.d2h):
+            out_host.copy_(y, non_blocking=True)
+        y.record_stream(self.d2h)  # keep the output's memory until the copy has read it
+
+    def synchronize(self) -> None:
+        self.d2h.synchronize()
+        torch.cuda.current_stream().synchronize()

@@ -103,3 +103,25 @@ def deepseek_weights():
     yield w
     del w
     torch.cuda.empty_cache()
+
+
+def test_host_pipeline_matches_direct_calls():
+    """HostPipeline (copies on their own streams, two device buffer sets)
+    gives each batch the output of a direct call on that batch."""
+    import layerstormexpertkernels_b200 as P
+    from layerstormexpertkernels_b200.synthetic import expert_weights, token_inputs
+    T, E, H, I = 96, 16, 256, 128
+    w_gu, w_down = expert_weights(E, H, I, device="cuda", seed_base=9000)
+    bias = token_inputs(1, E, 8, seed=3).bias.cuda()
+    layer = P.MoELayer(w_gu, w_down, bias, topk=4, n_group=4, topk_group=2)
+    batches = [token_inputs(T, E, H, seed=50 + i) for i in range(5)]
+    ins = [(b.hidden.pin_memory(), b.logits.pin_memory()) for b in batches]
+    outs = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in batches]
+    pipe = P.HostPipeline(lambda h, l: layer(h, l), (T, H), (T, E), torch.device("cuda"))
+    for (h, l), o in zip(ins, outs):
+        pipe.submit(h, l, o)
+    pipe.synchronize()
+    sync_and_check_device_error()
+    for b, o in zip(batches, outs):
+        ref = layer(b.hidden.cuda(), b.logits.cuda()).cpu()
+        assert torch.equal(o.view(torch.int16), ref.view(torch.int16))
