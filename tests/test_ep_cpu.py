@@ -259,3 +259,45 @@ def test_replicated_mode_loopback_threads(G):
     ref = canonical_layer(hidden, logits, bias, w_gu, w_down, topk=K_G, n_group=4, topk_group=2)
     for r in range(G):
         assert np.array_equal(outs[r].float().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+def _lost_rank_worker(rank, world, port, out_dir):
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:  # this rank leaves between layer calls, with nothing in flight
+        dist.destroy_process_group()
+        return
+    from ep_cpu_steps import CpuSteps
+    from layerstormexpertkernels_b200.ep import EPMoELayer
+    w_gu, w_down, bias, toks = _layer_inputs()
+    El = E_G // world
+    layer = EPMoELayer(torch.from_numpy(w_gu[:El]).to(torch.bfloat16),
+                       torch.from_numpy(w_down[:El]).to(torch.bfloat16), torch.from_numpy(bias),
+                       E_G, topk=K_G, n_group=4, topk_group=2, steps=CpuSteps)
+    hidden, logits = toks[0]
+    import time
+    t0 = time.time()
+    try:
+        layer(torch.from_numpy(hidden).to(torch.bfloat16), torch.from_numpy(logits))
+        outcome = "returned"
+    except RuntimeError as exc:
+        outcome = "error: " + type(exc).__name__
+    with open(os.path.join(out_dir, "lost.txt"), "w") as f:
+        f.write(f"{outcome} {time.time() - t0:.1f}")
+    try:
+        dist.destroy_process_group()
+    except Exception:  # noqa: BLE001 - the group is already broken
+        pass
+
+
+def test_ep_layer_lost_rank_raises_instead_of_hanging(tmp_path):
+    """A rank that leaves the group makes the next EP layer call on the
+    others fail with an error within the process-group timeout (5 s here),
+    not hang: the counts exchange is the first collective of the layer."""
+    mp.spawn(_lost_rank_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    outcome, seconds = (tmp_path / "lost.txt").read_text().rsplit(" ", 1)
+    assert outcome.startswith("error"), outcome
+    assert float(seconds) < 60
