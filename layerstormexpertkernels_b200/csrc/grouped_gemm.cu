@@ -80,15 +80,32 @@ constexpr int kBM = 128;                       // UMMA M, rows per tile
 constexpr int kBK = 64;                        // K per stage = one 128-byte swizzle row
 constexpr int kBN = 256;                       // UMMA N
 constexpr int kBoxRows = 128;                  // rows per TMA box
-constexpr int kStages = 4;
-constexpr int kABytes = kBM * kBK * 2;         // 16 KB
 constexpr int kBoxBytes = kBoxRows * kBK * 2;  // 16 KB
-constexpr int kStageBytes = kABytes + 2 * kBoxBytes;  // 48 KB
 constexpr int kTmemCols = 2 * kBN;             // two accumulators
 constexpr int kThreads = 192;
 constexpr int kMaxExperts = 1024;
 constexpr int kUnitQ = 4;                      // unit ids in flight between warps
 constexpr int kSwapMaxRows = 64;               // tiles this small use swapped operands
+
+// Pipeline geometry: ring stages, token rows loaded per k-block (the A box),
+// and the largest expert count the unit table holds.  Each stage holds the A
+// box and two 128-row weight boxes.
+template <int STAGES, int A_ROWS, int MAX_E>
+struct Geom {
+  static constexpr int kStages = STAGES;
+  static constexpr int kARows = A_ROWS;
+  static constexpr int kABytes = A_ROWS * kBK * 2;
+  static constexpr int kStageBytes = kABytes + 2 * kBoxBytes;
+  static constexpr int kMaxE = MAX_E;
+  // Every tile has at most kARows rows, so every tile is a swapped small tile.
+  static constexpr bool kSmallOnly = A_ROWS <= kSwapMaxRows;
+};
+// Any routing: 4 stages of 48 KB (128-row token box).
+using GeomFull = Geom<4, 128, kMaxExperts>;
+// Decode (every expert has at most 32 rows): a 32-row token box leaves room
+// for 6 stages of 36 KB, i.e. 192 KB of weights in flight instead of 128 KB.
+using GeomDecode = Geom<6, 32, 256>;
+constexpr int kDecodeMaxRows = GeomDecode::kARows;
 
 // M=128, N=256, A/B bf16 K-major, D fp32 (tcgen05 instruction descriptor:
 // D format bits 4-5, A format bits 7-9, B format bits 10-12, N>>3 bits 17-22,
@@ -126,10 +143,11 @@ struct Params {
 
 enum GemmMode : int { kModePlain = 0, kModeSwiglu = 1, kModeCombine = 2 };
 
-struct Smem {
-  uint8_t tiles[kStages][kStageBytes];  // 1024-byte aligned (base is aligned)
-  uint64_t full_bar[kStages];
-  uint64_t empty_bar[kStages];
+template <class G>
+struct SmemT {
+  uint8_t tiles[G::kStages][G::kStageBytes];  // 1024-byte aligned (base is aligned)
+  uint64_t full_bar[G::kStages];
+  uint64_t empty_bar[G::kStages];
   uint64_t acc_full_bar[2];
   uint64_t acc_empty_bar[2];
   uint64_t mma_done_bar;
@@ -139,11 +157,17 @@ struct Smem {
   uint32_t tmem_base;
   int32_t abort;
   int32_t warp_tot[kThreads / 32];
-  int32_t offs[kMaxExperts + 1];
-  int32_t cum[kMaxExperts + 1];
+  int32_t offs[G::kMaxE + 1];
+  int32_t cum[G::kMaxE + 1];
 };
-constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
-static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+template <class G>
+constexpr size_t smem_bytes() {
+  return sizeof(SmemT<G>) + 1024;
+}
+static_assert(smem_bytes<GeomFull>() <= 227 * 1024, "shared memory budget");
+static_assert(smem_bytes<GeomDecode>() <= 227 * 1024, "shared memory budget");
+static_assert(GeomDecode::kStageBytes % 1024 == 0 && GeomDecode::kABytes % 1024 == 0,
+              "swizzled boxes must start on 1024-byte boundaries");
 
 // ---- PTX wrappers ----------------------------------------------------------
 
@@ -267,13 +291,15 @@ __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
-__device__ __forceinline__ int mtiles_of(const Smem& s, int e) {
+template <class S>
+__device__ __forceinline__ int mtiles_of(const S& s, int e) {
   const int n = s.offs[e + 1] - s.offs[e];
   return n > 0 ? (n + kBM - 1) / kBM : 0;
 }
 
 // Valid rows of m-tile m of expert e (1..kBM).
-__device__ __forceinline__ int tile_rows(const Smem& s, int e, int m) {
+template <class S>
+__device__ __forceinline__ int tile_rows(const S& s, int e, int m) {
   const int left = s.offs[e + 1] - s.offs[e] - m * kBM;
   return left < kBM ? left : kBM;
 }
@@ -286,7 +312,8 @@ __device__ __forceinline__ uint32_t swap_idesc(int nn) {
 
 // Maps a unit id to (expert, m-tile, n-tile): the largest e with cum[e] <= id
 // is the (non-empty) expert that owns it.
-__device__ __forceinline__ void decode_unit(const Smem& s, int num_experts, int id, int& e,
+template <class S>
+__device__ __forceinline__ void decode_unit(const S& s, int num_experts, int id, int& e,
                                             int& m, int& n) {
   int lo = 0, hi = num_experts - 1;
   while (lo < hi) {
@@ -301,12 +328,16 @@ __device__ __forceinline__ void decode_unit(const Smem& s, int num_experts, int 
   m = local - n * mt;
 }
 
-template <int MODE>
+template <int MODE, class G>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                         const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ Params p) {
   constexpr bool SWIGLU = MODE == kModeSwiglu;
   constexpr bool COMBINE = MODE == kModeCombine;
+  using Smem = SmemT<G>;
+  constexpr int kStages = G::kStages;
+  constexpr int kStageBytes = G::kStageBytes;
+  constexpr int kABytes = G::kABytes;
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~static_cast<uintptr_t>(1023));
@@ -390,7 +421,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued = 0;
-      uint32_t last_phase[kStages] = {0, 0, 0, 0};
+      uint32_t last_phase[kStages];
+#pragma unroll
+      for (int st = 0; st < kStages; ++st) last_phase[st] = 0;
       bool ok = true;
       int qslot = 0;
       uint32_t qphase = 0;
@@ -457,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int e, m, n;
         decode_unit(s, E, unit, e, m, n);
         const int rows_here = tile_rows(s, e, m);
-        const bool swapped = rows_here <= kSwapMaxRows;
+        const bool swapped = G::kSmallOnly || rows_here <= kSwapMaxRows;
         const int nn = (rows_here + 15) & ~15;
         const uint32_t sw_idesc = swap_idesc(nn);
         const int acc = it & 1;
@@ -547,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         drow = p.D + static_cast<int64_t>(valid ? r : 0) * p.ldd + col0;
       }
-      if (rows_here <= kSwapMaxRows) {
+      if (G::kSmallOnly || rows_here <= kSwapMaxRows) {
         // Transposed accumulator: this thread's TMEM lane is weight row
         // w = 32q + lane of each box, columns [0, nn) hold box 0 for the
         // tile's tokens and [nn, 2nn) box 1.
@@ -686,14 +719,15 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D bf16 map over a [outer, inner] row-major tensor, box [kBoxRows, kBK],
+// 2-D bf16 map over a [outer, inner] row-major tensor, box [box_rows, kBK],
 // 128-byte swizzle, zero fill out of bounds.
-lsek_status make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer) {
+lsek_status make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                     uint32_t box_rows = kBoxRows) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return fail(LSEK_ERR_CUDA, "grouped_gemm: cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {inner * 2};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(kBoxRows)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t es[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
                         strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -704,20 +738,21 @@ lsek_status make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_
   return LSEK_OK;
 }
 
-template <int MODE>
-lsek_status launch(void* D, const void* A, const void* B, const int32_t* offsets, int E, int rows,
-                   int n_out, int b_rows, int K, float limit, int32_t* counter, cudaStream_t st,
-                   const Params* combine = nullptr) {
+template <int MODE, class G>
+lsek_status launch_geom(void* D, const void* A, const void* B, const int32_t* offsets, int E,
+                        int rows, int n_out, int b_rows, int K, float limit, int32_t* counter,
+                        cudaStream_t st, const Params* combine) {
   constexpr bool SWIGLU = MODE == kModeSwiglu;
   static PerDeviceOnce attrs;
   const cudaError_t ae = once_per_device(attrs, [] {
-    return cudaFuncSetAttribute(grouped_gemm_kernel<MODE>,
+    return cudaFuncSetAttribute(grouped_gemm_kernel<MODE, G>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(kSmemBytes));
+                                static_cast<int>(smem_bytes<G>()));
   });
   if (ae != cudaSuccess) return fail(LSEK_ERR_CUDA, "grouped_gemm: %s", cudaGetErrorString(ae));
   CUtensorMap ma, mb;
-  lsek_status s = make_map(&ma, A, static_cast<uint64_t>(K), static_cast<uint64_t>(rows));
+  lsek_status s = make_map(&ma, A, static_cast<uint64_t>(K), static_cast<uint64_t>(rows),
+                           static_cast<uint32_t>(G::kARows));
   if (s != LSEK_OK) return s;
   s = make_map(&mb, B, static_cast<uint64_t>(K), static_cast<uint64_t>(E) * b_rows);
   if (s != LSEK_OK) return s;
@@ -748,9 +783,23 @@ lsek_status launch(void* D, const void* A, const void* B, const int32_t* offsets
   const int64_t max_units = (ceil_div(rows, kBM) + E) * static_cast<int64_t>(p.n_tiles);
   const int grid = static_cast<int>(max_units < num_sms() ? max_units : num_sms());
   if (MODE == kModeCombine) LSEK_CUDA_TRY(cudaMemsetAsync(p.done, 0, sizeof(uint32_t), st));
-  grouped_gemm_kernel<MODE><<<grid, kThreads, kSmemBytes, st>>>(ma, mb, p);
+  grouped_gemm_kernel<MODE, G><<<grid, kThreads, smem_bytes<G>(), st>>>(ma, mb, p);
   return check_launch(SWIGLU ? "grouped_gemm_swiglu_bf16"
                              : (MODE == kModeCombine ? "ep_down_gemm_combine" : "grouped_gemm_bf16"));
+}
+
+// max_rows_per_expert: an upper bound on the rows of any expert (or -1 if
+// unknown); at most kDecodeMaxRows selects the decode geometry.
+template <int MODE>
+lsek_status launch(void* D, const void* A, const void* B, const int32_t* offsets, int E, int rows,
+                   int n_out, int b_rows, int K, float limit, int32_t* counter, cudaStream_t st,
+                   const Params* combine = nullptr, int max_rows_per_expert = -1) {
+  const int bound = rows <= kDecodeMaxRows ? rows : max_rows_per_expert;
+  if (bound >= 0 && bound <= kDecodeMaxRows && E <= GeomDecode::kMaxE)
+    return launch_geom<MODE, GeomDecode>(D, A, B, offsets, E, rows, n_out, b_rows, K, limit,
+                                         counter, st, combine);
+  return launch_geom<MODE, GeomFull>(D, A, B, offsets, E, rows, n_out, b_rows, K, limit, counter,
+                                     st, combine);
 }
 
 lsek_status validate(const char* name, const void* D, const void* A, const void* B,
@@ -772,17 +821,21 @@ lsek_status validate(const char* name, const void* D, const void* A, const void*
 }  // namespace gemm
 
 // Used by the layer forward.  `counter` is one zero-able int32 of device
-// scratch for dynamic unit scheduling, or null for the static stride.
+// scratch for dynamic unit scheduling, or null for the static stride;
+// `max_rows_per_expert` an upper bound on any expert's rows, or -1.
 lsek_status grouped_gemm_plain(void* D, const void* A, const void* B, const int32_t* offsets, int E,
-                               int rows, int N, int K, int32_t* counter, cudaStream_t st) {
+                               int rows, int N, int K, int32_t* counter, cudaStream_t st,
+                               int max_rows_per_expert) {
   if (rows == 0 || N == 0) return LSEK_OK;
-  return gemm::launch<gemm::kModePlain>(D, A, B, offsets, E, rows, N, N, K, 0.0f, counter, st);
+  return gemm::launch<gemm::kModePlain>(D, A, B, offsets, E, rows, N, N, K, 0.0f, counter, st,
+                                        nullptr, max_rows_per_expert);
 }
 lsek_status grouped_gemm_swiglu(void* H, const void* A, const void* Wgu, const int32_t* offsets,
                                 int E, int rows, int I, int K, float limit, int32_t* counter,
-                                cudaStream_t st) {
+                                cudaStream_t st, int max_rows_per_expert) {
   if (rows == 0 || I == 0) return LSEK_OK;
-  return gemm::launch<gemm::kModeSwiglu>(H, A, Wgu, offsets, E, rows, I, 2 * I, K, limit, counter, st);
+  return gemm::launch<gemm::kModeSwiglu>(H, A, Wgu, offsets, E, rows, I, 2 * I, K, limit, counter,
+                                         st, nullptr, max_rows_per_expert);
 }
 
 }  // namespace lsek
@@ -820,7 +873,7 @@ extern "C" lsek_status lsek_grouped_gemm_bf16(void* D, const void* A, const void
                "grouped_gemm_bf16: workspace must be 4-byte aligned");
   return grouped_gemm_plain(D, A, B, expert_offsets, num_experts, rows, N, K,
                             gemm_counter(workspace, workspace_bytes),
-                            static_cast<cudaStream_t>(stream));
+                            static_cast<cudaStream_t>(stream), -1);
 }
 
 extern "C" lsek_status lsek_grouped_gemm_swiglu_bf16(void* Hout, const void* A, const void* W_gu,
@@ -839,7 +892,7 @@ extern "C" lsek_status lsek_grouped_gemm_swiglu_bf16(void* Hout, const void* A, 
                "grouped_gemm_swiglu_bf16: workspace must be 4-byte aligned");
   return grouped_gemm_swiglu(Hout, A, W_gu, expert_offsets, num_experts, rows, I, K, swiglu_limit,
                              gemm_counter(workspace, workspace_bytes),
-                             static_cast<cudaStream_t>(stream));
+                             static_cast<cudaStream_t>(stream), -1);
 }
 
 extern "C" lsek_status lsek_ep_down_gemm_combine(lsek_ep_domain* h, const void* hact,

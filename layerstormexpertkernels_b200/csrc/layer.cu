@@ -18,10 +18,11 @@ lsek_status launch_route(const int32_t* idx, int64_t n, int E, int32_t* offsets,
 lsek_status launch_permute_rows(void* dst, const void* src, const int32_t* s2d, int64_t T,
                                 int topk, int64_t row_bytes, cudaStream_t st);
 lsek_status grouped_gemm_plain(void* D, const void* A, const void* B, const int32_t* offsets,
-                               int E, int rows, int N, int K, int32_t* counter, cudaStream_t st);
+                               int E, int rows, int N, int K, int32_t* counter, cudaStream_t st,
+                               int max_rows_per_expert);
 lsek_status grouped_gemm_swiglu(void* H, const void* A, const void* Wgu, const int32_t* offsets,
                                 int E, int rows, int I, int K, float limit, int32_t* counter,
-                                cudaStream_t st);
+                                cudaStream_t st, int max_rows_per_expert);
 
 namespace {
 struct LayerWs {
@@ -108,12 +109,13 @@ extern "C" lsek_status lsek_moe_layer_forward(
   s = launch_permute_rows(x, hidden, s2d, T, k, static_cast<int64_t>(hidden_dim) * 2, st);
   if (s != LSEK_OK) return s;
   if ((s = mark(3)) != LSEK_OK) return s;
+  // The top-k experts of a token are distinct, so no expert gets more than T rows.
   s = grouped_gemm_swiglu(h, x, W_gu, offs, E, static_cast<int>(n), inter_dim, hidden_dim,
-                          swiglu_limit, counter, st);
+                          swiglu_limit, counter, st, T);
   if (s != LSEK_OK) return s;
   if ((s = mark(4)) != LSEK_OK) return s;
   s = grouped_gemm_plain(x, h, W_down, offs, E, static_cast<int>(n), hidden_dim, inter_dim,
-                         counter, st);
+                         counter, st, T);
   if (s != LSEK_OK) return s;
   if ((s = mark(5)) != LSEK_OK) return s;
   s = lsek_moe_unpermute(out, x, w, s2d, T, k, hidden_dim, LSEK_BF16, 0, stream);

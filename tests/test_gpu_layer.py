@@ -125,3 +125,22 @@ def test_host_pipeline_matches_direct_calls():
     for b, o in zip(batches, outs):
         ref = layer(b.hidden.cuda(), b.logits.cuda()).cpu()
         assert torch.equal(o.view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("T_small", [1, 7, 32])
+def test_decode_geometry_matches_full_geometry(deepseek_weights, T_small):
+    """T <= 32 runs the GEMMs with the decode pipeline geometry (32-row token
+    box, six stages); a token's output depends only on its own routing, so
+    the first tokens of a larger call (full geometry) must have the same
+    bits."""
+    import layerstormexpertkernels_b200 as P
+    from layerstormexpertkernels_b200.synthetic import token_inputs
+    w_gu, w_down = deepseek_weights
+    x = token_inputs(80, 256, 7168, seed=77)
+    bias = x.bias.cuda()
+    big = P.moe_layer_forward(x.hidden.cuda(), x.logits.cuda(), bias, w_gu, w_down, 8, 8, 4, 2.5,
+                              True)
+    small = P.moe_layer_forward(x.hidden[:T_small].cuda(), x.logits[:T_small].cuda(), bias, w_gu,
+                                w_down, 8, 8, 4, 2.5, True)
+    sync_and_check_device_error()
+    assert torch.equal(small.view(torch.int16), big[:T_small].view(torch.int16))
