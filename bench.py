@@ -48,7 +48,6 @@ UNIT = "tokens/s"
 WORKLOAD = ("cfg1: DeepSeek-V3 routed MoE layer forward (gating, permute, gate/up GEMM + "
             "SwiGLU, down GEMM, weighted unpermute), T=4096 tokens/GPU, H=7168, I=2048, "
             "E=256, top-8, 8 groups / 4 kept, bf16 weights")
-LAUNCHES_PER_STEP = 6  # gating, route, row copy, gate/up GEMM, down GEMM, unpermute
 STAGES = ("gating", "route", "row_copy", "gate_up_swiglu_gemm", "down_gemm", "unpermute")
 
 
@@ -357,7 +356,8 @@ def run_ours(args):
                        "hidden": HIDDEN, "inter": INTER, "experts": E, "topk": TOPK,
                        "parallelism": "replicas" if world > 1 else "single",
                        "l2": "inputs larger than L2: 22.5 GB of expert weights per step"},
-            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+            # gating, route (1 or 3 kernels), row copy, gate/up GEMM, down GEMM, unpermute
+            "gpu_launches": (5 + route_launches(T * TOPK)) * args.steps,
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": T * HIDDEN * 2 + T * E * 4,
                     "d2h_bytes_per_step": T * HIDDEN * 2,
