@@ -143,3 +143,41 @@ def test_workspace_sizes(lib):
     ws = lib.lsek_moe_layer_workspace_size(4096, 7168, 2048, 256, 8)
     # at least X [T*k,H] + Hact [T*k,I] in bf16
     assert ws >= 4096 * 8 * (7168 + 2048) * 2
+
+
+def test_ep_entry_points_reject_bad_arguments(lib):
+    """The expert-parallel entry points validate before any CUDA call."""
+    d = ctypes.c_void_p(16)
+    z = ctypes.c_size_t(0)
+    f = lib.lsek_ep_plan
+    # world size 0, experts not a multiple of the world size, topk out of range
+    assert f(d, d, d, d, d, 4, 8, 64, 0, d, z, None) == LSEK_ERR_INVALID_ARG
+    assert f(d, d, d, d, d, 4, 8, 60, 8, d, z, None) == LSEK_ERR_INVALID_ARG
+    assert f(d, d, d, d, d, 4, 33, 64, 8, d, z, None) == LSEK_ERR_INVALID_ARG
+    assert f(d, d, d, d, d, 4, 8, 64, 65, d, z, None) == LSEK_ERR_INVALID_ARG
+    # hidden_dim must be a multiple of 8
+    g = lib.lsek_ep_dispatch_pack
+    assert g(d, d, d, 4, d, d, d, d, d, 4, 8, 12, 64, 8, None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_ep_slot_scan(d, d, -1, 8, None) == LSEK_ERR_INVALID_ARG
+    h = lib.lsek_ep_expert_permute
+    assert h(d, 4, d, d, d, d, d, 4, 8, 64, 0, d, z, None) == LSEK_ERR_INVALID_ARG  # 0 local experts
+    assert lib.lsek_ep_combine_pack(d, -1, d, d, d, d, d, 4, 8, 64, None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_ep_combine_reduce(d, d, -1, d, d, d, 4, 8, 64, 64, 8, None) == LSEK_ERR_INVALID_ARG
+
+
+def test_ep_domain_entry_points_reject_bad_arguments(lib):
+    out = ctypes.c_void_p()
+    create = lib.lsek_ep_domain_create
+    assert create(ctypes.byref(out), 0, 17, 64, 64, 8) == LSEK_ERR_INVALID_ARG   # world > 16
+    assert create(ctypes.byref(out), 2, 2, 64, 64, 8) == LSEK_ERR_INVALID_ARG    # rank >= world
+    assert create(ctypes.byref(out), 0, 2, 64, 60, 8) == LSEK_ERR_INVALID_ARG    # H % 8
+    assert create(ctypes.byref(out), 0, 2, 0, 64, 8) == LSEK_ERR_INVALID_ARG     # no tokens
+    assert out.value is None
+    assert lib.lsek_ep_domain_export(None, ctypes.c_void_p(16), ctypes.c_size_t(64)) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_ep_wait(None, 0, 1, 0, None) == LSEK_ERR_INVALID_ARG
+    lib.lsek_ep_domain_bytes.restype = ctypes.c_size_t
+    one = lib.lsek_ep_domain_bytes(8192, 7168, 8, 8)
+    # control block + recv rows [T*G, H] + ids / weights [T*G, k] + combine rows [T*k, H]
+    assert one >= 4096 + 8192 * 8 * 7168 * 2 + 2 * 8192 * 8 * 8 * 4 + 8192 * 8 * 7168 * 2
+    assert lib.lsek_ep_domain_bytes(-1, 7168, 8, 8) == 0
+    lib.lsek_ep_domain_destroy(None)  # a no-op
