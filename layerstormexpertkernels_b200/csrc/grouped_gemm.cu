@@ -129,6 +129,10 @@ struct Params {
   int n_out;               // output width
   float swiglu_limit;
   int32_t* counter;        // zeroed unit counter in device memory, or null (static stride)
+  // Gathered A: row r of the (virtual) permuted A is row gather_idx[r] / gather_k
+  // of the tensor behind tmap_a (the token rows), loaded with tile::gather4.
+  const int32_t* gather_idx;
+  int gather_k;
   // COMBINE mode
   const int32_t* dst_rank;  // [rows] rank whose combine buffer receives row p
   const int32_t* dst_row;   // [rows] row there
@@ -157,6 +161,7 @@ struct SmemT {
   uint32_t tmem_base;
   int32_t abort;
   int32_t warp_tot[kThreads / 32];
+  int32_t arow[kBM];  // gathered A: source row of each tile row (producer only)
   int32_t offs[G::kMaxE + 1];
   int32_t cum[G::kMaxE + 1];
 };
@@ -219,6 +224,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+// Four rows (row coordinates y0..y3, one 128-byte box row each) of a tensor
+// whose map has a one-row box, stored back to back at `dst`.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int y0, int y1, int y2, int y3,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(y0), "r"(y1), "r"(y2),
+      "r"(y3), "l"(policy)
       : "memory");
 }
 __device__ __forceinline__ uint64_t policy_evict_normal() {
@@ -445,14 +462,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         decode_unit(s, E, unit, e, m, n);
         const int row0 = s.offs[e] + m * kBM;
         const int brow = e * p.b_rows + n * p.b_tile_rows;
+        // Gathered A: the MMA reads 128 rows (or, for a swapped small tile,
+        // its rows rounded up to 16); rows past the expert repeat its first
+        // row (their results are discarded).
+        int nload = 0;
+        if (p.gather_idx != nullptr) {
+          const int valid = min(kBM, s.offs[e + 1] - row0);
+          nload = (G::kSmallOnly || valid <= kSwapMaxRows) ? ((valid + 15) & ~15) : kBM;
+          for (int r = 0; r < nload; ++r)
+            s.arow[r] = __ldg(p.gather_idx + row0 + (r < valid ? r : 0)) / p.gather_k;
+        }
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&s.empty_bar[stage], phase ^ 1u, abort, kDevErrGemmProducerWait, true)) {
             ok = false;
             break;
           }
           uint8_t* a = s.tiles[stage];
-          mbar_expect_tx(&s.full_bar[stage], kStageBytes);
-          tma_load_2d(a, &tmap_a, &s.full_bar[stage], kb * kBK, row0, pol_a);
+          if (p.gather_idx != nullptr) {
+            mbar_expect_tx(&s.full_bar[stage], static_cast<uint32_t>(nload * kBK * 2 + 2 * kBoxBytes));
+            for (int r = 0; r < nload; r += 4)
+              tma_gather4(a + r * kBK * 2, &tmap_a, &s.full_bar[stage], kb * kBK, s.arow[r],
+                          s.arow[r + 1], s.arow[r + 2], s.arow[r + 3], pol_a);
+          } else {
+            mbar_expect_tx(&s.full_bar[stage], kStageBytes);
+            tma_load_2d(a, &tmap_a, &s.full_bar[stage], kb * kBK, row0, pol_a);
+          }
           tma_load_2d(a + kABytes, &tmap_b, &s.full_bar[stage], kb * kBK, brow, pol_w);
           tma_load_2d(a + kABytes + kBoxBytes, &tmap_b, &s.full_bar[stage], kb * kBK,
                       brow + p.b_second, pol_w);
@@ -738,10 +772,18 @@ lsek_status make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_
   return LSEK_OK;
 }
 
+// Gathered A (gather_idx non-null): A is the [a_rows, K] token tensor and row r
+// of the permuted A is A[gather_idx[r] / gather_k]; `rows` counts permuted rows.
+struct Gather {
+  const int32_t* idx = nullptr;
+  int k = 1;
+  int a_rows = 0;
+};
+
 template <int MODE, class G>
 lsek_status launch_geom(void* D, const void* A, const void* B, const int32_t* offsets, int E,
                         int rows, int n_out, int b_rows, int K, float limit, int32_t* counter,
-                        cudaStream_t st, const Params* combine) {
+                        cudaStream_t st, const Params* combine, const Gather& gather) {
   constexpr bool SWIGLU = MODE == kModeSwiglu;
   static PerDeviceOnce attrs;
   const cudaError_t ae = once_per_device(attrs, [] {
@@ -751,8 +793,11 @@ lsek_status launch_geom(void* D, const void* A, const void* B, const int32_t* of
   });
   if (ae != cudaSuccess) return fail(LSEK_ERR_CUDA, "grouped_gemm: %s", cudaGetErrorString(ae));
   CUtensorMap ma, mb;
-  lsek_status s = make_map(&ma, A, static_cast<uint64_t>(K), static_cast<uint64_t>(rows),
-                           static_cast<uint32_t>(G::kARows));
+  lsek_status s =
+      gather.idx != nullptr
+          ? make_map(&ma, A, static_cast<uint64_t>(K), static_cast<uint64_t>(gather.a_rows), 1u)
+          : make_map(&ma, A, static_cast<uint64_t>(K), static_cast<uint64_t>(rows),
+                     static_cast<uint32_t>(G::kARows));
   if (s != LSEK_OK) return s;
   s = make_map(&mb, B, static_cast<uint64_t>(K), static_cast<uint64_t>(E) * b_rows);
   if (s != LSEK_OK) return s;
@@ -768,6 +813,8 @@ lsek_status launch_geom(void* D, const void* A, const void* B, const int32_t* of
   p.b_rows = b_rows;
   p.swiglu_limit = limit;
   p.counter = counter;
+  p.gather_idx = gather.idx;
+  p.gather_k = gather.k;
   if (counter != nullptr) LSEK_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(int32_t), st));
   if (SWIGLU) {
     p.n_tiles = static_cast<int>(ceil_div(n_out, kBoxRows));
@@ -793,13 +840,14 @@ lsek_status launch_geom(void* D, const void* A, const void* B, const int32_t* of
 template <int MODE>
 lsek_status launch(void* D, const void* A, const void* B, const int32_t* offsets, int E, int rows,
                    int n_out, int b_rows, int K, float limit, int32_t* counter, cudaStream_t st,
-                   const Params* combine = nullptr, int max_rows_per_expert = -1) {
+                   const Params* combine = nullptr, int max_rows_per_expert = -1,
+                   const Gather& gather = Gather()) {
   const int bound = rows <= kDecodeMaxRows ? rows : max_rows_per_expert;
   if (bound >= 0 && bound <= kDecodeMaxRows && E <= GeomDecode::kMaxE)
     return launch_geom<MODE, GeomDecode>(D, A, B, offsets, E, rows, n_out, b_rows, K, limit,
-                                         counter, st, combine);
+                                         counter, st, combine, gather);
   return launch_geom<MODE, GeomFull>(D, A, B, offsets, E, rows, n_out, b_rows, K, limit, counter,
-                                     st, combine);
+                                     st, combine, gather);
 }
 
 lsek_status validate(const char* name, const void* D, const void* A, const void* B,
@@ -836,6 +884,21 @@ lsek_status grouped_gemm_swiglu(void* H, const void* A, const void* Wgu, const i
   if (rows == 0 || I == 0) return LSEK_OK;
   return gemm::launch<gemm::kModeSwiglu>(H, A, Wgu, offsets, E, rows, I, 2 * I, K, limit, counter,
                                          st, nullptr, max_rows_per_expert);
+}
+// The same with the permute folded into the A load: permuted row r is
+// hidden[permuted_idx[r] / topk] (hidden has num_tokens rows).
+lsek_status grouped_gemm_swiglu_gather(void* H, const void* hidden, const void* Wgu,
+                                       const int32_t* offsets, const int32_t* permuted_idx,
+                                       int num_tokens, int topk, int E, int rows, int I, int K,
+                                       float limit, int32_t* counter, cudaStream_t st,
+                                       int max_rows_per_expert) {
+  if (rows == 0 || I == 0) return LSEK_OK;
+  gemm::Gather g;
+  g.idx = permuted_idx;
+  g.k = topk;
+  g.a_rows = num_tokens;
+  return gemm::launch<gemm::kModeSwiglu>(H, hidden, Wgu, offsets, E, rows, I, 2 * I, K, limit,
+                                         counter, st, nullptr, max_rows_per_expert, g);
 }
 
 }  // namespace lsek

@@ -1,5 +1,6 @@
-// Whole routed-expert layer on one stream: gating -> route + row copy ->
-// gate/up GEMM with SwiGLU epilogue -> down GEMM -> weighted unpermute.
+// Whole routed-expert layer on one stream: gating -> route -> row copy into
+// expert order (folded into the GEMM's own TMA loads for small T) -> gate/up
+// GEMM with SwiGLU epilogue -> down GEMM -> weighted unpermute.
 // The composition is the reference's documented expert flow (USAGE.md:40-57);
 // ref_expert_forward (tests/test_reference.py:257-276) is its oracle for
 // top-1, generalised here to top-k slots.
@@ -15,14 +16,19 @@ namespace lsek {
 size_t permute_workspace_bytes(int64_t n_keys, int num_experts);
 lsek_status launch_route(const int32_t* idx, int64_t n, int E, int32_t* offsets, int32_t* s2d,
                          int32_t* perm, void* ws, cudaStream_t st);
-lsek_status launch_permute_rows(void* dst, const void* src, const int32_t* s2d, int64_t T,
-                                int topk, int64_t row_bytes, cudaStream_t st);
 lsek_status grouped_gemm_plain(void* D, const void* A, const void* B, const int32_t* offsets,
                                int E, int rows, int N, int K, int32_t* counter, cudaStream_t st,
                                int max_rows_per_expert);
 lsek_status grouped_gemm_swiglu(void* H, const void* A, const void* Wgu, const int32_t* offsets,
                                 int E, int rows, int I, int K, float limit, int32_t* counter,
                                 cudaStream_t st, int max_rows_per_expert);
+lsek_status launch_permute_rows(void* dst, const void* src, const int32_t* s2d, int64_t T,
+                                int topk, int64_t row_bytes, cudaStream_t st);
+lsek_status grouped_gemm_swiglu_gather(void* H, const void* hidden, const void* Wgu,
+                                       const int32_t* offsets, const int32_t* permuted_idx,
+                                       int num_tokens, int topk, int E, int rows, int I, int K,
+                                       float limit, int32_t* counter, cudaStream_t st,
+                                       int max_rows_per_expert);
 
 namespace {
 struct LayerWs {
@@ -76,6 +82,10 @@ extern "C" lsek_status lsek_moe_layer_forward(
   LSEK_REQUIRE(hidden_dim % 32 == 0 && inter_dim % 32 == 0,
                "moe_layer_forward: hidden_dim and inter_dim must be multiples of 32");
   LSEK_REQUIRE(out && hidden && logits && W_gu && W_down, "moe_layer_forward: NULL tensor pointer");
+  LSEK_REQUIRE(reinterpret_cast<uintptr_t>(hidden) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(W_gu) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(W_down) % 16 == 0,
+               "moe_layer_forward: hidden, W_gu and W_down must be 16-byte aligned");
   LSEK_REQUIRE(static_cast<int64_t>(T) * k < (1ll << 31), "moe_layer_forward: T*topk too large");
   const LayerWs l = layer_ws(T, hidden_dim, inter_dim, E, k);
   LSEK_REQUIRE(workspace != nullptr && workspace_bytes >= l.total,
@@ -105,13 +115,27 @@ extern "C" lsek_status lsek_moe_layer_forward(
   if ((s = lsek_topk_gating(w, idx, logits, bias, gp, stream)) != LSEK_OK) return s;
   if ((s = mark(1)) != LSEK_OK) return s;
   if ((s = launch_route(idx, n, E, offs, s2d, perm, ws + l.route, st)) != LSEK_OK) return s;
+  // The top-k experts of a token are distinct, so no expert gets more than T
+  // rows.  Up to kGatherMaxTokens tokens every tile is a small one, and the
+  // permute is folded into the gate/up GEMM's A load (a tile's few token rows
+  // gathered from `hidden` through permuted_idx, four per TMA gather), which
+  // saves the row-copy launch; above it the row copy feeds whole 128-row
+  // tiles to tiled TMA loads (gathering 128 rows per k-block costs the TMA
+  // unit more than the copy saves).
+  constexpr int kGatherMaxTokens = 64;
+  const bool gather = T <= kGatherMaxTokens;
   if ((s = mark(2)) != LSEK_OK) return s;
-  s = launch_permute_rows(x, hidden, s2d, T, k, static_cast<int64_t>(hidden_dim) * 2, st);
-  if (s != LSEK_OK) return s;
+  if (!gather) {
+    s = launch_permute_rows(x, hidden, s2d, T, k, static_cast<int64_t>(hidden_dim) * 2, st);
+    if (s != LSEK_OK) return s;
+  }
   if ((s = mark(3)) != LSEK_OK) return s;
-  // The top-k experts of a token are distinct, so no expert gets more than T rows.
-  s = grouped_gemm_swiglu(h, x, W_gu, offs, E, static_cast<int>(n), inter_dim, hidden_dim,
-                          swiglu_limit, counter, st, T);
+  if (gather)
+    s = grouped_gemm_swiglu_gather(h, hidden, W_gu, offs, perm, T, k, E, static_cast<int>(n),
+                                   inter_dim, hidden_dim, swiglu_limit, counter, st, T);
+  else
+    s = grouped_gemm_swiglu(h, x, W_gu, offs, E, static_cast<int>(n), inter_dim, hidden_dim,
+                            swiglu_limit, counter, st, T);
   if (s != LSEK_OK) return s;
   if ((s = mark(4)) != LSEK_OK) return s;
   s = grouped_gemm_plain(x, h, W_down, offs, E, static_cast<int>(n), hidden_dim, inter_dim,

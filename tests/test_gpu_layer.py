@@ -144,3 +144,21 @@ def test_decode_geometry_matches_full_geometry(deepseek_weights, T_small):
                                 w_down, 8, 8, 4, 2.5, True)
     sync_and_check_device_error()
     assert torch.equal(small.view(torch.int16), big[:T_small].view(torch.int16))
+
+
+@pytest.mark.parametrize("T_small", [16, 64])
+def test_gathered_rows_match_copied_rows(deepseek_weights, T_small):
+    """Up to 64 tokens the layer gathers the token rows inside the gate/up
+    GEMM (TMA gather of four rows); larger calls copy them first.  Same bits
+    for the tokens both calls share."""
+    import layerstormexpertkernels_b200 as P
+    from layerstormexpertkernels_b200.synthetic import token_inputs
+    w_gu, w_down = deepseek_weights
+    x = token_inputs(160, 256, 7168, seed=91)
+    bias = x.bias.cuda()
+    big = P.moe_layer_forward(x.hidden.cuda(), x.logits.cuda(), bias, w_gu, w_down, 8, 8, 4, 2.5,
+                              True)
+    small = P.moe_layer_forward(x.hidden[:T_small].cuda(), x.logits[:T_small].cuda(), bias, w_gu,
+                                w_down, 8, 8, 4, 2.5, True)
+    sync_and_check_device_error()
+    assert torch.equal(small.view(torch.int16), big[:T_small].view(torch.int16))
