@@ -6,37 +6,49 @@
 // This is the contraction of ref_grouped_gemm (tests/test_reference.py:228-254)
 // and of the expert FFN flow in USAGE.md:40-57.
 //
-// Tiling.  A tile is 128 rows x 256 B-rows x all of K.  Work units are
-// (expert, n-tile, m-tile) in that nesting, m fastest, so the m-tiles that
-// share one weight tile are taken by neighbouring CTAs at the same time and
-// the weight tile is read from HBM once (the second read hits L2); the 16-28
-// n-tiles of one expert reuse its A rows from L2.  A persistent grid of one
-// CTA per SM takes units from an atomic counter in caller scratch (or, with
-// no scratch, with a static stride): CTAs that become free together take
-// neighbouring units, so the two m-tiles of an expert read each weight line
-// within microseconds of each other and the second read hits L2, where a
-// static stride lets the CTAs drift apart until the line has been evicted.
-// At DeepSeek-V3 shape the kernel is bound by streaming the weights from HBM.
+// Tiling.  A tile is 128 rows x 256 B-rows x all of K.  A work unit is one
+// n-tile of one expert against one m-tile or, when the expert has another
+// m-tile after it, against two m-tiles at once (a paired unit: M = 256 from
+// two MMAs that share every weight box, accumulating into both TMEM
+// accumulators).  Pairing halves the shared-memory fill of weight boxes for
+// experts with more than 128 rows; at DeepSeek-V3 shape (about 128 rows per
+// expert) half the experts have a short second tile, which without pairing
+// re-read the whole weight tile.  Units are (expert, n-tile, m-unit) in that
+// nesting, m fastest, so the m-units that share one weight tile are taken by
+// neighbouring CTAs at the same time and the weight tile is read from HBM
+// once (later reads hit L2); the 16-28 n-tiles of one expert reuse its A rows
+// from L2.  A persistent grid of one CTA per SM takes units from an atomic
+// counter in caller scratch (or, with no scratch, with a static stride):
+// CTAs that become free together take neighbouring units, so units that
+// share a weight tile read each line within microseconds of each other and
+// the later reads hit L2, where a static stride lets the CTAs drift apart
+// until the line has been evicted.  At DeepSeek-V3 shape the kernel is bound
+// by streaming the weights from HBM.
 //
 // One CTA = 6 warps:
 //   warp 0      TMA producer: takes the next unit id, publishes it to the
 //               other warps through a 4-entry shared-memory queue, then per
-//               k-block loads A [128 x 64] and two B boxes [128 x 64] into a
-//               4-stage ring (128-byte swizzle), completing on the stage's
-//               `full` mbarrier.
-//   warp 1      MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=16) per stage into
-//               one of two TMEM accumulators (2 x 256 fp32 columns = all 512
-//               columns); tcgen05.commit frees the stage and, after the last
-//               k-block, signals the accumulator full.
+//               k-block loads one stage (two weight boxes [128 x 64] and the
+//               A box [128 x 64], or two A boxes for a paired unit) into a
+//               208 KB byte ring (128-byte swizzle), completing on the
+//               stage's `full` mbarrier.  Single stages (48 KB) and paired
+//               ones (64 KB) share the ring back to back.
+//   warp 1      MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=16) per stage
+//               and accumulator, into one of two TMEM accumulators (2 x 256
+//               fp32 columns = all 512 columns), or both for a paired unit;
+//               tcgen05.commit frees the stage and, after the last k-block,
+//               signals each accumulator full.
 //   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM
 //               lanes 32*(w%4)..+31 = its 32 rows), convert, store to global,
-//               then release the accumulator; it overlaps the next tile's
-//               main loop thanks to the second accumulator.
-// Small tiles (at most kSwapMaxRows valid rows: the tail of an expert with
-// 129..192 rows, or every tile at decode sizes) swap the operands: the two
-// weight boxes become the MMA's M side (2 x M=128) and the tile's r token
-// rows its N side (N = r rounded up to 16), so the tensor-core work scales
-// with r instead of a full 128-row tile.  The epilogue of such a tile reads
+//               then release the accumulator; a single unit's epilogue
+//               overlaps the next unit's main loop thanks to the second
+//               accumulator (a paired unit waits for both).
+// Small unpaired tiles (at most kSwapMaxRows valid rows: experts of at most
+// 64 rows, the last tile of an expert with an odd tile count, every tile at
+// decode sizes) swap the operands: the two weight boxes become the MMA's M
+// side (2 x M=128) and the tile's r token rows its N side (N = r rounded up
+// to 16), so the tensor-core work scales with r instead of a full 128-row
+// tile.  The epilogue of such a tile reads
 // the transposed accumulator (TMEM lane = output column, TMEM column =
 // token).  The same products are summed in the same k order either way.
 // COMBINE mode (the expert-parallel down projection) ends each output row
@@ -87,24 +99,41 @@ constexpr int kMaxExperts = 1024;
 constexpr int kUnitQ = 4;                      // unit ids in flight between warps
 constexpr int kSwapMaxRows = 64;               // tiles this small use swapped operands
 
-// Pipeline geometry: ring stages, token rows loaded per k-block (the A box),
-// and the largest expert count the unit table holds.  Each stage holds the A
-// box and two 128-row weight boxes.
-template <int STAGES, int A_ROWS, int MAX_E>
+// Pipeline geometry.  Each k-block of a unit is one stage: its A box (token
+// rows; two A boxes for a paired unit) followed by two 128-row weight boxes.
+// Stages are laid out back to back in a byte ring of RING_BYTES, so a paired
+// unit's larger stages and a single unit's smaller ones share the ring
+// without padding; each stage has one full and one empty barrier (a ring of
+// kRecs records).  A box starting near the end of the ring continues at its
+// start, so the ring length must keep every box whole: a multiple of the box
+// size (full geometry), or of the one stage size when every stage is alike.
+// A_ROWS is the token rows of the A box, MAX_E the largest expert count the
+// unit table holds.
+template <int RING_BYTES, int A_ROWS, int MAX_E>
 struct Geom {
-  static constexpr int kStages = STAGES;
+  static constexpr int kRingBytes = RING_BYTES;
   static constexpr int kARows = A_ROWS;
   static constexpr int kABytes = A_ROWS * kBK * 2;
-  static constexpr int kStageBytes = kABytes + 2 * kBoxBytes;
+  static constexpr int kStageBytes = kABytes + 2 * kBoxBytes;  // a single unit's stage
+  static constexpr int kPairStageBytes = 2 * kABytes + 2 * kBoxBytes;
   static constexpr int kMaxE = MAX_E;
+  static constexpr int kRecs = 8;  // more than the stages that fit in the ring
   // Every tile has at most kARows rows, so every tile is a swapped small tile.
   static constexpr bool kSmallOnly = A_ROWS <= kSwapMaxRows;
+  // Units may cover two m-tiles of an expert (M = 256 against one weight tile).
+  static constexpr bool kPairs = !kSmallOnly;
+  static_assert(kABytes % 1024 == 0, "swizzled boxes start on 1024-byte boundaries");
+  static_assert(kPairs ? (kABytes == kBoxBytes && RING_BYTES % kBoxBytes == 0)
+                       : RING_BYTES % kStageBytes == 0,
+                "every box must lie whole inside the ring");
+  static_assert(kRecs * kStageBytes > RING_BYTES, "a record is reused only after its stage left");
 };
-// Any routing: 4 stages of 48 KB (128-row token box).
-using GeomFull = Geom<4, 128, kMaxExperts>;
-// Decode (every expert has at most 32 rows): a 32-row token box leaves room
-// for 6 stages of 36 KB, i.e. 192 KB of weights in flight instead of 128 KB.
-using GeomDecode = Geom<6, 32, 256>;
+// Any routing: a 208 KB ring, four 48 KB single stages or three 64 KB paired
+// stages in flight.
+using GeomFull = Geom<13 * kBoxBytes, 128, kMaxExperts>;
+// Decode (every expert has at most 32 rows): a 4 KB token box, six 36 KB
+// stages in flight.
+using GeomDecode = Geom<6 * (4096 + 2 * kBoxBytes), 32, 256>;
 constexpr int kDecodeMaxRows = GeomDecode::kARows;
 
 // M=128, N=256, A/B bf16 K-major, D fp32 (tcgen05 instruction descriptor:
@@ -149,9 +178,9 @@ enum GemmMode : int { kModePlain = 0, kModeSwiglu = 1, kModeCombine = 2 };
 
 template <class G>
 struct SmemT {
-  uint8_t tiles[G::kStages][G::kStageBytes];  // 1024-byte aligned (base is aligned)
-  uint64_t full_bar[G::kStages];
-  uint64_t empty_bar[G::kStages];
+  uint8_t ring[G::kRingBytes];  // 1024-byte aligned (base is aligned)
+  uint64_t full_bar[G::kRecs];
+  uint64_t empty_bar[G::kRecs];
   uint64_t acc_full_bar[2];
   uint64_t acc_empty_bar[2];
   uint64_t mma_done_bar;
@@ -171,8 +200,6 @@ constexpr size_t smem_bytes() {
 }
 static_assert(smem_bytes<GeomFull>() <= 227 * 1024, "shared memory budget");
 static_assert(smem_bytes<GeomDecode>() <= 227 * 1024, "shared memory budget");
-static_assert(GeomDecode::kStageBytes % 1024 == 0 && GeomDecode::kABytes % 1024 == 0,
-              "swizzled boxes must start on 1024-byte boundaries");
 
 // ---- PTX wrappers ----------------------------------------------------------
 
@@ -314,6 +341,14 @@ __device__ __forceinline__ int mtiles_of(const S& s, int e) {
   return n > 0 ? (n + kBM - 1) / kBM : 0;
 }
 
+// Units of one n-tile of expert e: one per m-tile, or with pairing one per
+// two m-tiles (the last one alone when the count is odd).
+template <class S>
+__device__ __forceinline__ int munits_of(const S& s, int e, bool pairs) {
+  const int mt = mtiles_of(s, e);
+  return pairs ? (mt + 1) >> 1 : mt;
+}
+
 // Valid rows of m-tile m of expert e (1..kBM).
 template <class S>
 __device__ __forceinline__ int tile_rows(const S& s, int e, int m) {
@@ -327,23 +362,70 @@ __device__ __forceinline__ uint32_t swap_idesc(int nn) {
          (static_cast<uint32_t>(kBM >> 4) << 24);
 }
 
-// Maps a unit id to (expert, m-tile, n-tile): the largest e with cum[e] <= id
-// is the (non-empty) expert that owns it.
+// A work unit: n-tile n of expert e against m-tile t0 and, when paired,
+// m-tile t0 + 1 too; both m-tiles multiply the same weight boxes.
+struct Unit {
+  int e, n, t0;
+  bool pair;
+};
+
+// Maps a unit id to its unit: the largest e with cum[e] <= id is the
+// (non-empty) expert that owns it; an expert's units are ordered
+// (n-tile, m-unit) with the m-unit fastest.
 template <class S>
-__device__ __forceinline__ void decode_unit(const S& s, int num_experts, int id, int& e,
-                                            int& m, int& n) {
+__device__ __forceinline__ Unit decode_unit(const S& s, int num_experts, int id, bool pairs) {
   int lo = 0, hi = num_experts - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (s.cum[mid] <= id) lo = mid;
     else hi = mid - 1;
   }
-  e = lo;
-  const int local = id - s.cum[e];
-  const int mt = mtiles_of(s, e);
-  n = local / mt;
-  m = local - n * mt;
+  Unit u;
+  u.e = lo;
+  const int local = id - s.cum[lo];
+  const int mu = munits_of(s, lo, pairs);
+  u.n = local / mu;
+  const int m = local - u.n * mu;
+  u.t0 = pairs ? 2 * m : m;
+  u.pair = pairs && u.t0 + 1 < mtiles_of(s, lo);
+  return u;
 }
+
+// Position in the stage ring: stage j uses record j % kRecs (barrier parity
+// (j / kRecs) & 1) and starts at byte `off` of the ring.  Producer and MMA
+// issuer walk the same stage sequence and each keeps its own copy.
+template <class G>
+struct RingPos {
+  uint32_t j = 0;    // stages so far
+  uint32_t off = 0;  // ring offset of stage j
+  __device__ __forceinline__ int rec() const { return static_cast<int>(j % G::kRecs); }
+  __device__ __forceinline__ uint32_t parity() const { return (j / G::kRecs) & 1u; }
+  // Ring address of byte `at` of the current stage.
+  __device__ __forceinline__ uint32_t at(uint32_t at_off) const {
+    const uint32_t o = off + at_off;
+    return o >= static_cast<uint32_t>(G::kRingBytes) ? o - G::kRingBytes : o;
+  }
+  __device__ __forceinline__ void advance(uint32_t bytes) {
+    ++j;
+    off = at(bytes);
+  }
+  // Ring offsets of the current stage's boxes.  The two weight boxes go
+  // first and stay adjacent, so one N=256 MMA reads both; when the stage
+  // starts in the ring's last box the first A box takes that box and the
+  // weight boxes start the next lap.  A1 is the second A box of a paired
+  // unit.
+  __device__ __forceinline__ void layout(uint32_t& a0, uint32_t& a1, uint32_t& b0) const {
+    if (off + kBoxBytes == static_cast<uint32_t>(G::kRingBytes)) {
+      a0 = off;
+      b0 = 0;
+      a1 = 2u * kBoxBytes;
+    } else {
+      b0 = off;
+      a0 = at(2u * kBoxBytes);
+      a1 = at(2u * kBoxBytes + G::kABytes);
+    }
+  }
+};
 
 template <int MODE, class G>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -352,16 +434,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool SWIGLU = MODE == kModeSwiglu;
   constexpr bool COMBINE = MODE == kModeCombine;
   using Smem = SmemT<G>;
-  constexpr int kStages = G::kStages;
-  constexpr int kStageBytes = G::kStageBytes;
-  constexpr int kABytes = G::kABytes;
+  constexpr int kRecs = G::kRecs;
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int E = p.num_experts;
+  // Pairing reads the second m-tile through the tiled A map, so a gathered A
+  // keeps one m-tile per unit.
+  const bool pairs = G::kPairs && p.gather_idx == nullptr;
 
-  // ---- unit table: cum[e] = sum over e' < e of m-tiles(e') * n_tiles -------
+  // ---- unit table: cum[e] = sum over e' < e of m-units(e') * n_tiles -------
   // Offsets are clamped to [0, rows]; an expert whose end precedes its start
   // has no tiles, so every stored row stays inside D.
   for (int i = tid; i <= E; i += kThreads) {
@@ -376,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int eb = tid * per;
     const int ee = min(E, eb + per);
     int local = 0;
-    for (int e = eb; e < ee; ++e) local += mtiles_of(s, e) * p.n_tiles;
+    for (int e = eb; e < ee; ++e) local += munits_of(s, e, pairs) * p.n_tiles;
     int incl = local;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
@@ -389,13 +472,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = 0; w < warp; ++w) run += s.warp_tot[w];
     for (int e = eb; e < ee; ++e) {
       s.cum[e] = run;
-      run += mtiles_of(s, e) * p.n_tiles;
+      run += munits_of(s, e, pairs) * p.n_tiles;
     }
     if (eb < E && ee == E) s.cum[E] = run;
   }
 
   if (warp == 0 && lane == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < kRecs; ++i) {
       mbar_init(&s.full_bar[i], 1);
       mbar_init(&s.empty_bar[i], 1);
     }
@@ -430,20 +513,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ===================== TMA producer =====================
     if (lane == 0) {
-      // Weights: normal eviction, so the other m-tiles of an expert, which
+      // Weights: normal eviction, so the other m-units of an expert, which
       // read the same weight tile moments later, find it in L2 (an
       // evict-first hint made them re-read it from HBM: 4-9 % slower).
       const uint64_t pol_w = policy_evict_normal();
       const uint64_t pol_a = policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued = 0;
-      uint32_t last_phase[kStages];
-#pragma unroll
-      for (int st = 0; st < kStages; ++st) last_phase[st] = 0;
+      RingPos<G> pos;
+      uint32_t j_free = 0;        // stages before this one have been released
+      uint32_t held = 0;          // ring bytes of stages j_free .. pos.j - 1
+      uint32_t paired = 0;        // bit r: record r's outstanding stage is a paired unit's
       bool ok = true;
       int qslot = 0;
       uint32_t qphase = 0;
+      // Reserves `bytes` of ring for the next stage: releases the oldest
+      // stages (waiting for the MMA to free them) until the stage and its
+      // record are free, then arms its full barrier for `tx` bytes.  False
+      // on abort.
+      auto reserve = [&](uint32_t bytes, uint32_t tx) -> bool {
+        while (pos.j - j_free >= static_cast<uint32_t>(kRecs) ||
+               held + bytes > static_cast<uint32_t>(G::kRingBytes)) {
+          const int r = static_cast<int>(j_free % kRecs);
+          if (!mbar_wait(&s.empty_bar[r], (j_free / kRecs) & 1u, abort, kDevErrGemmProducerWait,
+                         true))
+            return false;
+          held -= ((paired >> r) & 1u) ? G::kPairStageBytes : G::kStageBytes;
+          ++j_free;
+        }
+        const uint32_t bit = 1u << pos.rec();
+        paired = bytes == static_cast<uint32_t>(G::kPairStageBytes) ? (paired | bit) : (paired & ~bit);
+        held += bytes;
+        mbar_expect_tx(&s.full_bar[pos.rec()], tx);
+        return true;
+      };
       for (int i = 0; ok; ++i) {
         if (!mbar_wait(&s.q_empty[qslot], qphase ^ 1u, abort, kDevErrGemmProducerWait, true)) {
           ok = false;
@@ -458,61 +559,61 @@ __global__ void __launch_bounds__(kThreads, 1)
           qphase ^= 1u;
         }
         if (unit < 0) break;
-        int e, m, n;
-        decode_unit(s, E, unit, e, m, n);
-        const int row0 = s.offs[e] + m * kBM;
-        const int brow = e * p.b_rows + n * p.b_tile_rows;
+        const Unit u = decode_unit(s, E, unit, pairs);
+        const int row0 = s.offs[u.e] + u.t0 * kBM;
+        const int brow = u.e * p.b_rows + u.n * p.b_tile_rows;
         // Gathered A: the MMA reads 128 rows (or, for a swapped small tile,
         // its rows rounded up to 16); rows past the expert repeat its first
         // row (their results are discarded).
         int nload = 0;
         if (p.gather_idx != nullptr) {
-          const int valid = min(kBM, s.offs[e + 1] - row0);
+          const int valid = min(kBM, s.offs[u.e + 1] - row0);
           nload = (G::kSmallOnly || valid <= kSwapMaxRows) ? ((valid + 15) & ~15) : kBM;
           for (int r = 0; r < nload; ++r)
             s.arow[r] = __ldg(p.gather_idx + row0 + (r < valid ? r : 0)) / p.gather_k;
         }
+        const uint32_t a_bytes =
+            p.gather_idx != nullptr ? static_cast<uint32_t>(nload * kBK * 2) : G::kABytes;
+        const uint32_t stage_bytes = u.pair ? G::kPairStageBytes : G::kStageBytes;
+        const uint32_t tx = a_bytes + (u.pair ? G::kABytes : 0u) + 2u * kBoxBytes;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&s.empty_bar[stage], phase ^ 1u, abort, kDevErrGemmProducerWait, true)) {
+          if (!reserve(stage_bytes, tx)) {
             ok = false;
             break;
           }
-          uint8_t* a = s.tiles[stage];
+          uint64_t* full = &s.full_bar[pos.rec()];
+          uint32_t oa0, oa1, ob0;
+          pos.layout(oa0, oa1, ob0);
+          uint8_t* a0 = s.ring + oa0;
           if (p.gather_idx != nullptr) {
-            mbar_expect_tx(&s.full_bar[stage], static_cast<uint32_t>(nload * kBK * 2 + 2 * kBoxBytes));
             for (int r = 0; r < nload; r += 4)
-              tma_gather4(a + r * kBK * 2, &tmap_a, &s.full_bar[stage], kb * kBK, s.arow[r],
-                          s.arow[r + 1], s.arow[r + 2], s.arow[r + 3], pol_a);
+              tma_gather4(a0 + r * kBK * 2, &tmap_a, full, kb * kBK, s.arow[r], s.arow[r + 1],
+                          s.arow[r + 2], s.arow[r + 3], pol_a);
           } else {
-            mbar_expect_tx(&s.full_bar[stage], kStageBytes);
-            tma_load_2d(a, &tmap_a, &s.full_bar[stage], kb * kBK, row0, pol_a);
+            tma_load_2d(a0, &tmap_a, full, kb * kBK, row0, pol_a);
           }
-          tma_load_2d(a + kABytes, &tmap_b, &s.full_bar[stage], kb * kBK, brow, pol_w);
-          tma_load_2d(a + kABytes + kBoxBytes, &tmap_b, &s.full_bar[stage], kb * kBK,
-                      brow + p.b_second, pol_w);
-          issued |= 1u << stage;
-          last_phase[stage] = phase;
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          if (u.pair) tma_load_2d(s.ring + oa1, &tmap_a, full, kb * kBK, row0 + kBM, pol_a);
+          tma_load_2d(s.ring + ob0, &tmap_b, full, kb * kBK, brow, pol_w);
+          tma_load_2d(s.ring + ob0 + kBoxBytes, &tmap_b, full, kb * kBK, brow + p.b_second, pol_w);
+          pos.advance(stage_bytes);
         }
       }
       if (!ok) {  // let every issued load land before the CTA can exit
-        for (int st = 0; st < kStages; ++st)
-          if (issued & (1u << st))
-            mbar_wait(&s.full_bar[st], last_phase[st], abort, kDevErrGemmProducerWait, false);
+        for (uint32_t j = j_free; j < pos.j; ++j)
+          mbar_wait(&s.full_bar[j % kRecs], (j / kRecs) & 1u, abort, kDevErrGemmProducerWait,
+                    false);
       }
     }
   } else if (warp == 1) {
     // ===================== MMA issuer =====================
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
+      RingPos<G> pos;
+      uint32_t ac = 0;  // accumulators taken so far (slot ac & 1, lap parity (ac >> 1) & 1)
       bool ok = true;
       int qslot = 0;
       uint32_t qphase = 0;
-      for (int it = 0; ok; ++it) {
+      const uint32_t ring = smem_u32(s.ring);
+      while (ok) {
         if (!mbar_wait(&s.q_full[qslot], qphase, abort, kDevErrGemmMmaWait, true)) break;
         const int unit = s.unit_q[qslot];
         mbar_arrive(&s.q_empty[qslot]);
@@ -521,50 +622,68 @@ __global__ void __launch_bounds__(kThreads, 1)
           qphase ^= 1u;
         }
         if (unit < 0) break;
-        int e, m, n;
-        decode_unit(s, E, unit, e, m, n);
-        const int rows_here = tile_rows(s, e, m);
-        const bool swapped = G::kSmallOnly || rows_here <= kSwapMaxRows;
+        const Unit u = decode_unit(s, E, unit, pairs);
+        const int rows_here = tile_rows(s, u.e, u.t0);
+        const bool swapped = !u.pair && (G::kSmallOnly || rows_here <= kSwapMaxRows);
         const int nn = (rows_here + 15) & ~15;
         const uint32_t sw_idesc = swap_idesc(nn);
-        const int acc = it & 1;
-        const uint32_t acc_phase = (it >> 1) & 1;
-        if (!mbar_wait(&s.acc_empty_bar[acc], acc_phase ^ 1u, abort, kDevErrGemmMmaWait, true)) {
+        const int acc0 = static_cast<int>(ac & 1u);
+        const int acc1 = static_cast<int>((ac + 1) & 1u);
+        if (!mbar_wait(&s.acc_empty_bar[acc0], ((ac >> 1) & 1u) ^ 1u, abort, kDevErrGemmMmaWait,
+                       true) ||
+            (u.pair && !mbar_wait(&s.acc_empty_bar[acc1], (((ac + 1) >> 1) & 1u) ^ 1u, abort,
+                                  kDevErrGemmMmaWait, true))) {
           ok = false;
           break;
         }
+        ac += u.pair ? 2u : 1u;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        const uint32_t d0 = tmem_base + static_cast<uint32_t>(acc0 * kBN);
+        const uint32_t d1 = tmem_base + static_cast<uint32_t>(acc1 * kBN);
+        const uint32_t stage_bytes = u.pair ? G::kPairStageBytes : G::kStageBytes;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&s.full_bar[stage], phase, abort, kDevErrGemmMmaWait, true)) {
+          const int rec = pos.rec();
+          if (!mbar_wait(&s.full_bar[rec], pos.parity(), abort, kDevErrGemmMmaWait, true)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(s.tiles[stage]);
-          const uint32_t b_addr = a_addr + kABytes;
+          uint32_t oa0, oa1, ob0;
+          pos.layout(oa0, oa1, ob0);
+          const uint32_t a0_addr = ring + oa0;
+          const uint32_t a1_addr = ring + oa1;
+          const uint32_t b0_addr = ring + ob0;
+          const uint32_t b1_addr = b0_addr + kBoxBytes;
           if (swapped) {
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk) {
-              const uint64_t tok = smem_desc_sw128(a_addr + kk * 32);
+              const uint64_t tok = smem_desc_sw128(a0_addr + kk * 32);
               const uint32_t acc_in = (kb | kk) != 0 ? 1u : 0u;
-              umma_bf16(d_tmem, smem_desc_sw128(b_addr + kk * 32), tok, sw_idesc, acc_in);
-              umma_bf16(d_tmem + static_cast<uint32_t>(nn),
-                        smem_desc_sw128(b_addr + kBoxBytes + kk * 32), tok, sw_idesc, acc_in);
+              umma_bf16(d0, smem_desc_sw128(b0_addr + kk * 32), tok, sw_idesc, acc_in);
+              umma_bf16(d0 + static_cast<uint32_t>(nn), smem_desc_sw128(b1_addr + kk * 32), tok,
+                        sw_idesc, acc_in);
             }
           } else {
+            // One N=256 MMA per K step against both (adjacent) weight boxes;
+            // all K steps of one accumulator before the other's.
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk)
-              umma_bf16(d_tmem, smem_desc_sw128(a_addr + kk * 32),
-                        smem_desc_sw128(b_addr + kk * 32), kIdesc, (kb | kk) != 0 ? 1u : 0u);
+              umma_bf16(d0, smem_desc_sw128(a0_addr + kk * 32), smem_desc_sw128(b0_addr + kk * 32),
+                        kIdesc, (kb | kk) != 0 ? 1u : 0u);
+            if (u.pair) {
+#pragma unroll
+              for (int kk = 0; kk < kBK / 16; ++kk)
+                umma_bf16(d1, smem_desc_sw128(a1_addr + kk * 32),
+                          smem_desc_sw128(b0_addr + kk * 32), kIdesc, (kb | kk) != 0 ? 1u : 0u);
+            }
           }
-          umma_commit(&s.empty_bar[stage]);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          umma_commit(&s.empty_bar[rec]);
+          pos.advance(stage_bytes);
         }
-        if (ok) umma_commit(&s.acc_full_bar[acc]);
+        if (ok) {
+          umma_commit(&s.acc_full_bar[acc0]);
+          if (u.pair) umma_commit(&s.acc_full_bar[acc1]);
+        }
       }
       // Outstanding MMAs read shared memory and write TMEM: finish them first.
       umma_commit(&s.mma_done_bar);
@@ -575,7 +694,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int qslot = 0;
     uint32_t qphase = 0;
-    for (int it = 0;; ++it) {
+    uint32_t ac = 0;
+    bool running = true;
+    while (running) {
       if (!mbar_wait(&s.q_full[qslot], qphase, abort, kDevErrGemmEpilogueWait, true)) break;
       const int unit = s.unit_q[qslot];
       __syncwarp();
@@ -585,134 +706,141 @@ __global__ void __launch_bounds__(kThreads, 1)
         qphase ^= 1u;
       }
       if (unit < 0) break;
-      const int acc = it & 1;
-      const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait(&s.acc_full_bar[acc], acc_phase, abort, kDevErrGemmEpilogueWait, true)) break;
-      tc_fence_after();
-      int e, m, n;
-      decode_unit(s, E, unit, e, m, n);
-      const int rows_here = tile_rows(s, e, m);
-      const int row0 = s.offs[e] + m * kBM;
-      const int r = row0 + q * 32 + lane;
-      const bool valid = r < s.offs[e + 1];
-      const uint32_t tbase =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kBN);
-      const int col0 = n * p.out_tile_cols;
-      const int cols_here = min(p.out_tile_cols, p.n_out - col0);
-      __nv_bfloat16* drow = nullptr;
-      float wrow = 1.0f;
-      bool live = valid;
-      if (COMBINE) {
-        if (valid) {
-          const int32_t rk = __ldg(p.dst_rank + r), dr = __ldg(p.dst_row + r);
-          live = rk >= 0 && rk < p.world && dr >= 0 && dr < p.back_rows;
-          if (live)
-            drow = reinterpret_cast<__nv_bfloat16*>(p.peers.base[rk] + p.back_offset) +
-                   static_cast<int64_t>(dr) * p.ldd + col0;
-          wrow = __ldg(p.dst_w + r);
+      const Unit u = decode_unit(s, E, unit, pairs);
+      const int e = u.e;
+      for (int ti = 0; ti < (u.pair ? 2 : 1); ++ti, ++ac) {
+        const int acc = static_cast<int>(ac & 1u);
+        if (!mbar_wait(&s.acc_full_bar[acc], (ac >> 1) & 1u, abort, kDevErrGemmEpilogueWait,
+                       true)) {
+          running = false;
+          break;
         }
-      } else {
-        drow = p.D + static_cast<int64_t>(valid ? r : 0) * p.ldd + col0;
+        tc_fence_after();
+        const int m = u.t0 + ti;
+        const int rows_here = tile_rows(s, e, m);
+        const bool swapped = !u.pair && (G::kSmallOnly || rows_here <= kSwapMaxRows);
+        const int row0 = s.offs[e] + m * kBM;
+        const int r = row0 + q * 32 + lane;
+        const bool valid = r < s.offs[e + 1];
+        const uint32_t tbase =
+            tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kBN);
+        const int col0 = u.n * p.out_tile_cols;
+        const int cols_here = min(p.out_tile_cols, p.n_out - col0);
+        __nv_bfloat16* drow = nullptr;
+        float wrow = 1.0f;
+        bool live = valid;
+        if (COMBINE) {
+          if (valid) {
+            const int32_t rk = __ldg(p.dst_rank + r), dr = __ldg(p.dst_row + r);
+            live = rk >= 0 && rk < p.world && dr >= 0 && dr < p.back_rows;
+            if (live)
+              drow = reinterpret_cast<__nv_bfloat16*>(p.peers.base[rk] + p.back_offset) +
+                     static_cast<int64_t>(dr) * p.ldd + col0;
+            wrow = __ldg(p.dst_w + r);
+          }
+        } else {
+          drow = p.D + static_cast<int64_t>(valid ? r : 0) * p.ldd + col0;
+        }
+        if (swapped) {
+          // Transposed accumulator: this thread's TMEM lane is weight row
+          // w = 32q + lane of each box, columns [0, nn) hold box 0 for the
+          // tile's tokens and [nn, 2nn) box 1.
+          const int nn = (rows_here + 15) & ~15;
+          const int w = q * 32 + lane;
+          __nv_bfloat16* dcol = COMBINE ? nullptr : p.D + static_cast<int64_t>(row0) * p.ldd + col0;
+#pragma unroll 1
+          for (int t0 = 0; t0 < nn; t0 += 16) {
+            uint32_t v0[16], v1[16];
+            tmem_ld16(tbase + t0, v0);
+            tmem_ld16(tbase + nn + t0, v1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int t = t0 + i;
+              if (t >= rows_here) break;
+              if (COMBINE) {
+                const int pr = row0 + t;
+                const int32_t rk = __ldg(p.dst_rank + pr), dr = __ldg(p.dst_row + pr);
+                if (rk < 0 || rk >= p.world || dr < 0 || dr >= p.back_rows) continue;
+                __nv_bfloat16* dst =
+                    reinterpret_cast<__nv_bfloat16*>(p.peers.base[rk] + p.back_offset) +
+                    static_cast<int64_t>(dr) * p.ldd + col0;
+                const float wt = __ldg(p.dst_w + pr);
+                if (w < cols_here)
+                  dst[w] = __float2bfloat16_rn(__fmul_rn(wt, round_bf16(__uint_as_float(v0[i]))));
+                if (kBoxRows + w < cols_here)
+                  dst[kBoxRows + w] =
+                      __float2bfloat16_rn(__fmul_rn(wt, round_bf16(__uint_as_float(v1[i]))));
+                continue;
+              }
+              __nv_bfloat16* dst = dcol + static_cast<int64_t>(t) * p.ldd;
+              if (SWIGLU) {
+                if (w < cols_here)
+                  dst[w] = __float2bfloat16_rn(swiglu_f32(round_bf16(__uint_as_float(v0[i])),
+                                                          round_bf16(__uint_as_float(v1[i])),
+                                                          p.swiglu_limit));
+              } else {
+                if (w < cols_here) dst[w] = __float2bfloat16_rn(__uint_as_float(v0[i]));
+                if (kBoxRows + w < cols_here)
+                  dst[kBoxRows + w] = __float2bfloat16_rn(__uint_as_float(v1[i]));
+              }
+            }
+          }
+        } else if (SWIGLU) {
+#pragma unroll 1
+          for (int c = 0; c < kBoxRows; c += 32) {
+            uint32_t g[32], u[32];
+            tmem_ld32(tbase + c, g);
+            tmem_ld32(tbase + kBoxRows + c, u);
+            tmem_ld_wait();
+            if (valid && c < cols_here) {
+              uint32_t packed[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float h0 = swiglu_f32(round_bf16(__uint_as_float(g[2 * j])),
+                                            round_bf16(__uint_as_float(u[2 * j])), p.swiglu_limit);
+                const float h1 = swiglu_f32(round_bf16(__uint_as_float(g[2 * j + 1])),
+                                            round_bf16(__uint_as_float(u[2 * j + 1])),
+                                            p.swiglu_limit);
+                packed[j] = pack_bf16x2(h0, h1);
+              }
+              uint4* dst = reinterpret_cast<uint4*>(drow + c);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                                    packed[4 * j + 3]);
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < kBN; c += 32) {
+            uint32_t v[32];
+            tmem_ld32(tbase + c, v);
+            tmem_ld_wait();
+            if (live && c < cols_here) {
+              uint32_t packed[16];
+              if (COMBINE) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                  packed[j] = pack_bf16x2(__fmul_rn(wrow, round_bf16(__uint_as_float(v[2 * j]))),
+                                          __fmul_rn(wrow, round_bf16(__uint_as_float(v[2 * j + 1]))));
+              } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                  packed[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+              }
+              uint4* dst = reinterpret_cast<uint4*>(drow + c);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                                    packed[4 * j + 3]);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.acc_empty_bar[acc]);
       }
-      if (G::kSmallOnly || rows_here <= kSwapMaxRows) {
-        // Transposed accumulator: this thread's TMEM lane is weight row
-        // w = 32q + lane of each box, columns [0, nn) hold box 0 for the
-        // tile's tokens and [nn, 2nn) box 1.
-        const int nn = (rows_here + 15) & ~15;
-        const int w = q * 32 + lane;
-        __nv_bfloat16* dcol = COMBINE ? nullptr : p.D + static_cast<int64_t>(row0) * p.ldd + col0;
-#pragma unroll 1
-        for (int t0 = 0; t0 < nn; t0 += 16) {
-          uint32_t v0[16], v1[16];
-          tmem_ld16(tbase + t0, v0);
-          tmem_ld16(tbase + nn + t0, v1);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int t = t0 + i;
-            if (t >= rows_here) break;
-            if (COMBINE) {
-              const int pr = row0 + t;
-              const int32_t rk = __ldg(p.dst_rank + pr), dr = __ldg(p.dst_row + pr);
-              if (rk < 0 || rk >= p.world || dr < 0 || dr >= p.back_rows) continue;
-              __nv_bfloat16* dst =
-                  reinterpret_cast<__nv_bfloat16*>(p.peers.base[rk] + p.back_offset) +
-                  static_cast<int64_t>(dr) * p.ldd + col0;
-              const float wt = __ldg(p.dst_w + pr);
-              if (w < cols_here)
-                dst[w] = __float2bfloat16_rn(__fmul_rn(wt, round_bf16(__uint_as_float(v0[i]))));
-              if (kBoxRows + w < cols_here)
-                dst[kBoxRows + w] =
-                    __float2bfloat16_rn(__fmul_rn(wt, round_bf16(__uint_as_float(v1[i]))));
-              continue;
-            }
-            __nv_bfloat16* dst = dcol + static_cast<int64_t>(t) * p.ldd;
-            if (SWIGLU) {
-              if (w < cols_here)
-                dst[w] = __float2bfloat16_rn(swiglu_f32(round_bf16(__uint_as_float(v0[i])),
-                                                        round_bf16(__uint_as_float(v1[i])),
-                                                        p.swiglu_limit));
-            } else {
-              if (w < cols_here) dst[w] = __float2bfloat16_rn(__uint_as_float(v0[i]));
-              if (kBoxRows + w < cols_here)
-                dst[kBoxRows + w] = __float2bfloat16_rn(__uint_as_float(v1[i]));
-            }
-          }
-        }
-      } else if (SWIGLU) {
-#pragma unroll 1
-        for (int c = 0; c < kBoxRows; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld32(tbase + c, g);
-          tmem_ld32(tbase + kBoxRows + c, u);
-          tmem_ld_wait();
-          if (valid && c < cols_here) {
-            uint32_t packed[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float h0 = swiglu_f32(round_bf16(__uint_as_float(g[2 * j])),
-                                          round_bf16(__uint_as_float(u[2 * j])), p.swiglu_limit);
-              const float h1 = swiglu_f32(round_bf16(__uint_as_float(g[2 * j + 1])),
-                                          round_bf16(__uint_as_float(u[2 * j + 1])),
-                                          p.swiglu_limit);
-              packed[j] = pack_bf16x2(h0, h1);
-            }
-            uint4* dst = reinterpret_cast<uint4*>(drow + c);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
-                                  packed[4 * j + 3]);
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < kBN; c += 32) {
-          uint32_t v[32];
-          tmem_ld32(tbase + c, v);
-          tmem_ld_wait();
-          if (live && c < cols_here) {
-            uint32_t packed[16];
-            if (COMBINE) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j)
-                packed[j] = pack_bf16x2(__fmul_rn(wrow, round_bf16(__uint_as_float(v[2 * j]))),
-                                        __fmul_rn(wrow, round_bf16(__uint_as_float(v[2 * j + 1]))));
-            } else {
-#pragma unroll
-              for (int j = 0; j < 16; ++j)
-                packed[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-            }
-            uint4* dst = reinterpret_cast<uint4*>(drow + c);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
-                                  packed[4 * j + 3]);
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.acc_empty_bar[acc]);
     }
   }
 

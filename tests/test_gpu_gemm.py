@@ -160,8 +160,35 @@ def test_tile_shape_does_not_change_results(swiglu):
     sync_and_check_device_error()
 
 
+@pytest.mark.parametrize("swiglu", [False, True])
+@pytest.mark.parametrize("K", [64, 576, 1024])
+def test_paired_tiles_match_single_tiles(swiglu, K):
+    """Experts with more than 128 rows run their m-tiles two at a time
+    against one weight tile (two accumulators); the rows must come out
+    bit-identical to the same rows computed one 128-row tile per expert.
+    The k-block counts (1, 9, 16) move the shared-memory ring's wrap point
+    through every box position."""
+    N = 512
+    g = torch.Generator().manual_seed(K + swiglu)
+    b = (torch.randn(1, N, K, generator=g) / np.sqrt(K)).to(torch.bfloat16).cuda()
+    for rows in (129, 200, 256, 257, 300, 384, 520):
+        a = torch.randn(rows, K, generator=g).to(torch.bfloat16).cuda()
+        off = torch.tensor([0, rows], dtype=torch.int32, device="cuda")
+        cuts = list(range(0, rows, 128)) + [rows]
+        split = torch.tensor(cuts, dtype=torch.int32, device="cuda")
+        bs = b.expand(len(cuts) - 1, N, K).contiguous()
+        if swiglu:
+            whole = ek().grouped_gemm_swiglu_bf16(a, b, off)
+            tiled = ek().grouped_gemm_swiglu_bf16(a, bs, split)
+        else:
+            whole = ek().grouped_gemm_bf16(a, b, off)
+            tiled = ek().grouped_gemm_bf16(a, bs, split)
+        sync_and_check_device_error()
+        assert torch.equal(whole, tiled), f"rows={rows}"
+
+
 def test_tail_tiles_of_large_experts():
-    # Experts with 129..192 rows end in a swapped tail tile.
+    # Experts with 129..192 rows: a full tile paired with a short one.
     a, b, off = make_problem([130, 192, 150, 129], 512, 256, seed=21)
     out = ek().grouped_gemm_bf16(a.cuda(), b.cuda(), off.cuda())
     sync_and_check_device_error()

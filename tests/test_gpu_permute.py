@@ -184,9 +184,10 @@ def check_swiglu(out, gate, up, limit):
     got = out.float().cpu().numpy().astype(np.float64)
     # One rounding to the 16-bit format of a value within a few fp32 ulps of
     # the exact result: at most one 16-bit ulp away from it.  Below 2^-100
-    # fp32's e^-g overflows for g < -88.7 and silu(g) flushes to 0, as the
-    # reference's torch F.silu does; the double-precision oracle keeps the
-    # tiny value, so those elements only need to be tiny.
+    # silu(g) flushes to 0 (the kernel's quotient once 1 + e^-g passes 2^126,
+    # g < -87; fp32's e^-g itself for g < -88.7, as in the reference's torch
+    # F.silu); the double-precision oracle keeps the tiny value, so those
+    # elements only need to be tiny.
     if out.dtype == torch.bfloat16:
         ulp = np.maximum(np.abs(ref) * 2.0 ** -7, 2.0 ** -100)
     else:
@@ -202,6 +203,18 @@ def test_swiglu_vs_oracle(N, d, limit, scale):
     up = rand_bf16((N, d), seed=N * d, scale=scale)
     out = ek().fused_swiglu(torch.cat([gate, up], 1).cuda(), swiglu_limit=limit)
     check_swiglu(out.cpu(), gate, up, limit)
+
+
+@pytest.mark.parametrize("name", ["plain", "clamp10", "edges"])
+def test_swiglu_golden(golden_dir, name):
+    # The reference's own ref_swiglu outputs (tests/golden/make_golden.py).
+    d = np.load(os.path.join(golden_dir, f"swiglu_{name}.npz"))
+    gate = torch.from_numpy(d["gate"]).to(torch.bfloat16)
+    up = torch.from_numpy(d["up"]).to(torch.bfloat16)
+    out = ek().fused_swiglu(torch.cat([gate, up], 1).cuda(), swiglu_limit=float(d["limit"]))
+    got = out.float().cpu().numpy().astype(np.float64)
+    ref = d["out"].astype(np.float64)
+    assert (np.abs(got - ref) <= np.maximum(np.abs(ref) * 2.0 ** -7, 2.0 ** -100)).all()
 
 
 def test_swiglu_fp16():
