@@ -25,7 +25,7 @@
 // until the line has been evicted.  At DeepSeek-V3 shape the kernel is bound
 // by streaming the weights from HBM.
 //
-// One CTA = 6 warps:
+// One CTA = 10 warps:
 //   warp 0      TMA producer: takes the next unit id, publishes it to the
 //               other warps through a 4-entry shared-memory queue, then per
 //               k-block loads one stage (two weight boxes [128 x 64] and the
@@ -38,11 +38,12 @@
 //               fp32 columns = all 512 columns), or both for a paired unit;
 //               tcgen05.commit frees the stage and, after the last k-block,
 //               signals each accumulator full.
-//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM
-//               lanes 32*(w%4)..+31 = its 32 rows), convert, store to global,
-//               then release the accumulator; a single unit's epilogue
-//               overlaps the next unit's main loop thanks to the second
-//               accumulator (a paired unit waits for both).
+//   warps 2-9   epilogue, two groups of four: tcgen05.ld 32 columns at a
+//               time (warp w reads TMEM lanes 32*(w%4)..+31 = its 32 rows;
+//               each group takes half of the columns), convert, store to
+//               global, then release the accumulator; a single unit's
+//               epilogue overlaps the next unit's main loop thanks to the
+//               second accumulator (a paired unit waits for both).
 // Small unpaired tiles (at most kSwapMaxRows valid rows: experts of at most
 // 64 rows, the last tile of an expert with an odd tile count, every tile at
 // decode sizes) swap the operands: the two weight boxes become the MMA's M
@@ -94,7 +95,8 @@ constexpr int kBN = 256;                       // UMMA N
 constexpr int kBoxRows = 128;                  // rows per TMA box
 constexpr int kBoxBytes = kBoxRows * kBK * 2;  // 16 KB
 constexpr int kTmemCols = 2 * kBN;             // two accumulators
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;                   // two groups of four, one warp per TMEM lane quarter each
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxExperts = 1024;
 constexpr int kUnitQ = 4;                      // unit ids in flight between warps
 constexpr int kSwapMaxRows = 64;               // tiles this small use swapped operands
@@ -484,12 +486,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.acc_full_bar[i], 1);
-      mbar_init(&s.acc_empty_bar[i], 4);
+      mbar_init(&s.acc_empty_bar[i], kEpiWarps);
     }
     mbar_init(&s.mma_done_bar, 1);
     for (int i = 0; i < kUnitQ; ++i) {
       mbar_init(&s.q_full[i], 1);
-      mbar_init(&s.q_empty[i], 1 + 4);  // MMA lane + four epilogue warps
+      mbar_init(&s.q_empty[i], 1 + kEpiWarps);  // MMA lane + every epilogue warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
@@ -690,8 +692,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&s.mma_done_bar, 0, abort, kDevErrGemmMmaWait, false);
     }
   } else {
-    // ===================== epilogue (warps 2..5) =====================
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // ===================== epilogue (warps 2..9) =====================
+    // Two groups of four warps split every accumulator's columns, so one
+    // tile drains in half the time and a paired unit's two tiles in the
+    // time of one.
+    const int q = warp & 3;           // TMEM lane quarter this warp may access
+    const int grp = (warp - 2) >> 2;  // column half this warp drains
     int qslot = 0;
     uint32_t qphase = 0;
     uint32_t ac = 0;
@@ -749,7 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int w = q * 32 + lane;
           __nv_bfloat16* dcol = COMBINE ? nullptr : p.D + static_cast<int64_t>(row0) * p.ldd + col0;
 #pragma unroll 1
-          for (int t0 = 0; t0 < nn; t0 += 16) {
+          for (int t0 = grp * 16; t0 < nn; t0 += 32) {
             uint32_t v0[16], v1[16];
             tmem_ld16(tbase + t0, v0);
             tmem_ld16(tbase + nn + t0, v1);
@@ -788,7 +794,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else if (SWIGLU) {
 #pragma unroll 1
-          for (int c = 0; c < kBoxRows; c += 32) {
+          for (int c = grp * (kBoxRows / 2); c < (grp + 1) * (kBoxRows / 2); c += 32) {
             uint32_t g[32], u[32];
             tmem_ld32(tbase + c, g);
             tmem_ld32(tbase + kBoxRows + c, u);
@@ -813,7 +819,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else {
 #pragma unroll 1
-          for (int c = 0; c < kBN; c += 32) {
+          for (int c = grp * (kBN / 2); c < (grp + 1) * (kBN / 2); c += 32) {
             uint32_t v[32];
             tmem_ld32(tbase + c, v);
             tmem_ld_wait();
