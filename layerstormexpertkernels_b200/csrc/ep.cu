@@ -187,12 +187,16 @@ __global__ void __launch_bounds__(kThreads) ep_combine_pack_kernel(
 // One CTA per (token, slice of H): out[t] = bf16(sum over slots j, in order,
 // of the returned combine row of (t, j)), fp32 from 0 - the fixed-order
 // reduce of moe_combine_reduce_slots_bf16_to_bf16.  A slot without a valid
-// expert adds +0.  Rows at or past comb_count are never read.
+// expert adds +0.  Rows at or past comb_count are never read.  K > 0 fixes
+// the slot count at compile time, so all K rows' loads are in flight before
+// the first add; K = 0 takes it from k.
+template <int K>
 __global__ void __launch_bounds__(kThreads) ep_combine_reduce_kernel(
     __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ comb,
     const int32_t* __restrict__ idx, const int32_t* __restrict__ pair_row,
-    const int32_t* __restrict__ slot_row, int32_t comb_count, int k, int H, int E, int G,
+    const int32_t* __restrict__ slot_row, int32_t comb_count, int k_rt, int H, int E, int G,
     int span) {
+  const int k = K > 0 ? K : k_rt;
   __shared__ int64_t s_src[32];
   const int t = blockIdx.x;
   const int per = E / G;
@@ -214,7 +218,19 @@ __global__ void __launch_bounds__(kThreads) ep_combine_reduce_kernel(
   const int v_end = min(nvec, (blockIdx.y + 1) * span);
   for (int v = blockIdx.y * span + threadIdx.x; v < v_end; v += kThreads) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < k; ++j) {
+    if (K > 0) {
+      uint4 raw[K > 0 ? K : 1];
+#pragma unroll
+      for (int j = 0; j < K; ++j)
+        raw[j] = s_src[j] >= 0 ? ldg_nc_v4(comb + s_src[j] * H + v * 8) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[j]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], __bfloat162float(e[q]));
+      }
+    }
+    for (int j = 0; K == 0 && j < k; ++j) {
       if (s_src[j] < 0) {
 #pragma unroll
         for (int q = 0; q < 8; ++q) acc[q] = __fadd_rn(acc[q], 0.0f);
@@ -392,14 +408,26 @@ __global__ void __launch_bounds__(kThreads) ep_combine_push_kernel(
     const __nv_bfloat16* src = y + static_cast<int64_t>(p) * H;
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peers.base[rk] + back_off) +
                          static_cast<int64_t>(dr) * H;
-    for (int v = threadIdx.x; v < nvec; v += kThreads) {
-      const uint4 raw = ldg_nc_v4(src + v * 8);
-      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
-      uint4 out;
-      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(&out);
+    // Eight 16-byte loads in flight per thread before the first store.
+    for (int v0 = threadIdx.x; v0 < nvec; v0 += 8 * kThreads) {
+      uint4 raw[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) o[q] = __float2bfloat16_rn(__fmul_rn(wt, __bfloat162float(e[q])));
-      *reinterpret_cast<uint4*>(dst + v * 8) = out;
+      for (int u = 0; u < 8; ++u) {
+        const int v = v0 + u * kThreads;
+        if (v < nvec) raw[u] = ldg_nc_v4(src + v * 8);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int v = v0 + u * kThreads;
+        if (v >= nvec) break;
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[u]);
+        uint4 out;
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(&out);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          o[q] = __float2bfloat16_rn(__fmul_rn(wt, __bfloat162float(e[q])));
+        *reinterpret_cast<uint4*>(dst + v * 8) = out;
+      }
     }
   }
   if (publish) grid_release_to_peers(peers, world, me, kCtrlCombineFlags, done, epoch);
@@ -564,7 +592,8 @@ extern "C" lsek_status lsek_ep_combine_reduce(void* out, const void* comb_rows,
   if (slices > max_slices) slices = max_slices;
   const int span = static_cast<int>(ceil_div(nvec, slices));
   const dim3 grid(num_tokens, static_cast<unsigned>(ceil_div(nvec, span)));
-  ep_combine_reduce_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  auto kernel = topk == 8 ? ep_combine_reduce_kernel<8> : ep_combine_reduce_kernel<0>;
+  kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(comb_rows), topk_indices,
       pair_row, slot_row, comb_count, topk, hidden_dim, num_experts, world_size, span);
   return check_launch("ep_combine_reduce");
