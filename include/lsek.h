@@ -367,6 +367,15 @@ LSEK_API lsek_status lsek_ep_dispatch_push(lsek_ep_domain* d, int32_t* send_ids,
                                   const float* topk_weights, const int32_t* pair_row,
                                   const int32_t* send_off, int32_t num_tokens,
                                   int32_t num_experts, uint32_t epoch, void* stream);
+/* Copies `bytes` (a multiple of 4) of device memory into page-locked host
+ * memory with a kernel that stores through the host buffer's device mapping,
+ * so the copy never queues behind a large device-to-host transfer on another
+ * stream (the copy engine serves those in order).  Used to read the
+ * expert-parallel counts while the previous batch's output is being copied
+ * out.  host_dst must be page-locked (cudaHostAlloc or cudaHostRegister);
+ * the data is in place once the stream has passed this call. */
+LSEK_API lsek_status lsek_copy_to_mapped_host(void* host_dst, const void* dev_src, size_t bytes,
+                                              void* stream);
 /* Waits on the stream until every rank has published `epoch` for the
  * dispatch (what = 0) or the combine (what = 1); gives up after timeout_ns
  * (<= 0: 2 s) and records a device error. */

@@ -760,6 +760,37 @@ extern "C" lsek_status lsek_ep_dispatch_push(lsek_ep_domain* h, int32_t* send_id
   return check_launch("ep_dispatch_push");
 }
 
+namespace lsek {
+namespace {
+__global__ void copy_words_kernel(uint32_t* __restrict__ dst, const uint32_t* __restrict__ src,
+                                  int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = src[i];
+}
+}  // namespace
+}  // namespace lsek
+
+extern "C" lsek_status lsek_copy_to_mapped_host(void* host_dst, const void* dev_src, size_t bytes,
+                                                void* stream) {
+  LSEK_REQUIRE(bytes % 4 == 0, "copy_to_mapped_host: bytes must be a multiple of 4");
+  if (bytes == 0) return LSEK_OK;
+  LSEK_REQUIRE(host_dst && dev_src, "copy_to_mapped_host: NULL pointer");
+  LSEK_REQUIRE(reinterpret_cast<uintptr_t>(host_dst) % 4 == 0 &&
+                   reinterpret_cast<uintptr_t>(dev_src) % 4 == 0,
+               "copy_to_mapped_host: pointers must be 4-byte aligned");
+  void* mapped = nullptr;
+  if (cudaHostGetDevicePointer(&mapped, host_dst, 0) != cudaSuccess || mapped == nullptr) {
+    cudaGetLastError();  // the failed query leaves a (non-sticky) error behind: clear it
+    return fail(LSEK_ERR_INVALID_ARG, "copy_to_mapped_host: destination is not page-locked host memory");
+  }
+  const int64_t n = static_cast<int64_t>(bytes / 4);
+  const unsigned grid = static_cast<unsigned>(n < 256 * 64 ? ceil_div(n, 256) : 64);
+  copy_words_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint32_t*>(mapped), static_cast<const uint32_t*>(dev_src), n);
+  return check_launch("copy_to_mapped_host");
+}
+
 extern "C" lsek_status lsek_ep_wait(lsek_ep_domain* h, int32_t what, uint32_t epoch,
                                     int64_t timeout_ns, void* stream) {
   lsek_status s = domain_check(h, "ep_wait");

@@ -598,6 +598,18 @@ torch::Tensor ep_dispatch_push(int64_t h, torch::Tensor counts, torch::Tensor hi
   return send_ids;
 }
 
+void copy_to_mapped_host(torch::Tensor host_dst, torch::Tensor src) {
+  TORCH_CHECK(host_dst.device().is_cpu() && host_dst.is_pinned(),
+              "copy_to_mapped_host: host_dst must be a pinned CPU tensor");
+  TORCH_CHECK(src.is_cuda(), "copy_to_mapped_host: src must be a CUDA tensor");
+  TORCH_CHECK(host_dst.is_contiguous() && src.is_contiguous(),
+              "copy_to_mapped_host: tensors must be contiguous");
+  TORCH_CHECK(host_dst.nbytes() == src.nbytes(), "copy_to_mapped_host: sizes differ");
+  const c10::cuda::OptionalCUDAGuard guard(src.device());
+  check_status(lsek_copy_to_mapped_host(host_dst.data_ptr(), src.data_ptr(), src.nbytes(),
+                                        stream_of(src)));
+}
+
 void ep_wait(int64_t h, int64_t what, int64_t epoch, int64_t timeout_ns) {
   check_status(lsek_ep_wait(domain_of(h), to_i32(what, "what"), static_cast<uint32_t>(epoch),
                             timeout_ns, at::cuda::getCurrentCUDAStream().stream()));
@@ -777,6 +789,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_dispatch_push", &ep_dispatch_push, py::arg("domain"), py::arg("counts"),
         py::arg("hidden"), py::arg("topk_indices"), py::arg("topk_weights"), py::arg("pair_row"),
         py::arg("send_off"), py::arg("rows"), py::arg("num_experts"), py::arg("epoch"));
+  m.def("copy_to_mapped_host", &copy_to_mapped_host, py::arg("host_dst"), py::arg("src"));
   m.def("ep_wait", &ep_wait, py::arg("domain"), py::arg("what"), py::arg("epoch"),
         py::arg("timeout_ns") = 0);
   m.def("ep_combine_plan", &ep_combine_plan, py::arg("domain"), py::arg("s2d"),

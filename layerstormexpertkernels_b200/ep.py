@@ -178,6 +178,7 @@ class PeerDomain:
         (self.recv_rows, self.recv_ids, self.recv_w,
          self.back) = _C.ep_domain_buffers(self.handle, hidden_dim, topk)
         self.epoch = 0
+        self.mirror = HostMirror()
 
     def next_epoch(self) -> int:
         self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
@@ -223,13 +224,35 @@ class PeerDispatch:
         return int(self.counts[self.domain.rank, :, 1].sum())
 
 
+class HostMirror:
+    """Reads a small int32 device tensor into pinned host memory through a
+    kernel (lsek_copy_to_mapped_host) instead of a copy-engine transfer, so
+    the read never queues behind a large device-to-host copy of the previous
+    batch's output on another stream (HostPipeline)."""
+
+    def __init__(self):
+        self.buf = None
+        self.done = None
+
+    def read(self, src: torch.Tensor) -> torch.Tensor:
+        n = src.numel()
+        if self.buf is None or self.buf.numel() < n:
+            self.buf = torch.empty(n, dtype=torch.int32, pin_memory=True)
+            self.done = torch.cuda.Event()
+        host = self.buf[:n]
+        _C.copy_to_mapped_host(host, src.reshape(-1).contiguous())
+        self.done.record()
+        self.done.synchronize()
+        return host.clone().view(src.shape)
+
+
 def _gather_counts(send_counts: torch.Tensor, domain: PeerDomain) -> torch.Tensor:
     G = domain.world_size
     if G == 1:
-        return send_counts.reshape(1, 1, 2).cpu()
+        return domain.mirror.read(send_counts.reshape(1, 1, 2))
     every = torch.empty(G * G * 2, dtype=torch.int32, device=send_counts.device)
     dist.all_gather_into_tensor(every, send_counts.reshape(-1), group=domain.group)
-    return every.view(G, G, 2).cpu()
+    return domain.mirror.read(every.view(G, G, 2))
 
 
 def peer_dispatch(domain: PeerDomain, hidden: torch.Tensor, topk_indices: torch.Tensor,

@@ -181,3 +181,14 @@ def test_ep_domain_entry_points_reject_bad_arguments(lib):
     assert one >= 4096 + 8192 * 8 * 7168 * 2 + 2 * 8192 * 8 * 8 * 4 + 8192 * 8 * 7168 * 2
     assert lib.lsek_ep_domain_bytes(-1, 7168, 8, 8) == 0
     lib.lsek_ep_domain_destroy(None)  # a no-op
+
+
+def test_copy_to_mapped_host_rejects_bad_arguments(lib):
+    # All of these return before any CUDA call.
+    d = ctypes.c_void_p(16)
+    assert lib.lsek_copy_to_mapped_host(d, d, ctypes.c_size_t(6), None) == LSEK_ERR_INVALID_ARG
+    assert b"multiple of 4" in lib.lsek_last_error()
+    assert lib.lsek_copy_to_mapped_host(None, d, ctypes.c_size_t(8), None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_copy_to_mapped_host(d, ctypes.c_void_p(18), ctypes.c_size_t(8),
+                                        None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_copy_to_mapped_host(None, None, ctypes.c_size_t(0), None) == 0

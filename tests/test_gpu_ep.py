@@ -281,3 +281,27 @@ def test_ep_layer_two_gpus(tmp_path, transport):
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     for r in range(2):
         assert (tmp_path / f"ok{r}").read_text() == "bit-exact"
+
+
+def test_copy_to_mapped_host():
+    """The counts read used by the peer transport: a kernel stores through the
+    pinned buffer's device mapping, even while a large device-to-host copy
+    is queued on another stream."""
+    import layerstormexpertkernels_b200 as P
+    from layerstormexpertkernels_b200 import ep as EP
+    src = torch.arange(40, dtype=torch.int32, device="cuda") * 3 - 7
+    host = torch.zeros(40, dtype=torch.int32, pin_memory=True)
+    big = torch.randn(64 << 20, device="cuda")
+    big_h = torch.empty(big.shape, pin_memory=True)
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        big_h.copy_(big, non_blocking=True)
+    P._C.copy_to_mapped_host(host, src)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(host, src.cpu())
+    side.synchronize()
+    with pytest.raises(Exception):
+        P._C.copy_to_mapped_host(torch.zeros(40, dtype=torch.int32), src)  # pageable
+    mirror = EP.HostMirror()
+    got = mirror.read(src.view(5, 8))
+    assert got.shape == (5, 8) and torch.equal(got, src.view(5, 8).cpu())
