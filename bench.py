@@ -214,8 +214,15 @@ def host_pipeline_ms(forward, x, T, E, dev, steps, barrier, max_over_ranks):
     over ranks."""
     import torch
     import layerstormexpertkernels_b200 as P
-    hidden_h, logits_h = x.hidden.pin_memory(), x.logits.pin_memory()
-    outs_h = [torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    # Pinned buffers in this GPU's NUMA node (first touch under the GPU's
+    # cores); the process's own affinity is restored afterwards.
+    saved = os.sched_getaffinity(0)
+    P.bind_host_to_device(dev)
+    try:
+        hidden_h, logits_h = x.hidden.pin_memory(), x.logits.pin_memory()
+        outs_h = [torch.empty(T, HIDDEN, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    finally:
+        os.sched_setaffinity(0, saved)
     pipe = P.HostPipeline(forward, (T, HIDDEN), (T, E), dev)
     for i in range(2):
         pipe.submit(hidden_h, logits_h, outs_h[i % 2])

@@ -8,6 +8,7 @@ is its oracle for top-1 routing.
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -124,6 +125,36 @@ class MoELayer:
     __call__ = forward
 
 
+def bind_host_to_device(device=None) -> Optional[list]:
+    """Restricts the calling process to the CPU cores nearest `device` (the
+    GPU's CPU affinity from NVML), so page-locked host buffers allocated
+    afterwards live in the GPU's NUMA node and host<->device copies do not
+    cross the socket link.  Returns the cores, or None (nothing changed) when
+    NVML cannot tell.  Call it before allocating pinned buffers."""
+    try:
+        import pynvml
+        idx = torch.device(device).index if device is not None else None
+        if idx is None:
+            idx = torch.cuda.current_device()
+        props = torch.cuda.get_device_properties(idx)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            mask = pynvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        allowed = os.sched_getaffinity(0)
+        cores = [64 * w + b for w, m in enumerate(mask) for b in range(64)
+                 if (m >> b) & 1 and 64 * w + b in allowed]
+        if not cores:
+            return None
+        os.sched_setaffinity(0, cores)
+        return cores
+    except Exception:  # no NVML, no GPU, or an affinity the OS refuses
+        return None
+
+
 class HostPipeline:
     """Feeds a layer from pinned host memory with the copies overlapped.
 
@@ -135,7 +166,8 @@ class HostPipeline:
     computes, batch i+1 is being copied in and batch i-1 out.  Host buffers
     must be pinned; `out_host` holds its result after synchronize(), and an
     input host buffer can be refilled once the stream of the next submit()
-    has copied it (after synchronize(), at the latest).
+    has copied it (after synchronize(), at the latest).  Allocate the pinned
+    buffers after bind_host_to_device(), so they sit next to the GPU.
     """
 
     def __init__(self, forward, hidden_shape, logits_shape, device,

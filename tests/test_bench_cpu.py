@@ -33,3 +33,16 @@ def test_clock_summary_flags_throttle_reasons():
     out = s.summary()
     assert out["sm_mhz"] == (1965 + 1800) / 2 and out["sm_max_mhz"] == 1965
     assert out["reasons"] == ["sw_power_cap"] and out["samples"] == 2
+
+
+def test_bind_host_to_device_without_gpu_changes_nothing():
+    import os
+
+    import torch
+
+    import layerstormexpertkernels_b200 as P
+    if torch.cuda.is_available():
+        return  # the GPU tests exercise it
+    before = os.sched_getaffinity(0)
+    assert P.bind_host_to_device(None) is None
+    assert os.sched_getaffinity(0) == before

@@ -162,3 +162,17 @@ def test_gathered_rows_match_copied_rows(deepseek_weights, T_small):
                                 w_down, 8, 8, 4, 2.5, True)
     sync_and_check_device_error()
     assert torch.equal(small.view(torch.int16), big[:T_small].view(torch.int16))
+
+
+def test_bind_host_to_device():
+    import os
+
+    import layerstormexpertkernels_b200 as P
+    before = os.sched_getaffinity(0)
+    try:
+        cores = P.bind_host_to_device(torch.device("cuda", 0))
+        if cores is not None:
+            assert cores and set(cores) <= before
+            assert os.sched_getaffinity(0) == set(cores)
+    finally:
+        os.sched_setaffinity(0, before)
