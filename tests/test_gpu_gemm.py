@@ -193,3 +193,21 @@ def test_tail_tiles_of_large_experts():
     out = ek().grouped_gemm_bf16(a.cuda(), b.cuda(), off.cuda())
     sync_and_check_device_error()
     assert_close_bf16(out, oracle_gemm(a, b, off))
+
+
+def test_decode_down_projection_matches_full_geometry():
+    """A decode-sized down projection (at most 32 rows over a few experts,
+    N = 7168) runs the decode geometry; its rows must equal the same rows
+    computed by a full-geometry call, and the oracle."""
+    K, N = 2048, 7168
+    counts = [3, 0, 5, 1]
+    a, b, off = make_problem(counts + [40], K, N, seed=5, wscale=1.0 / np.sqrt(K))
+    a, b = a.cuda(), b.cuda()
+    small_off = off[:len(counts) + 1].cuda()
+    rows = int(sum(counts))
+    small = ek().grouped_gemm_bf16(a[:rows].contiguous(), b[:len(counts)].contiguous(), small_off)
+    full = ek().grouped_gemm_bf16(a, b, off.cuda())
+    sync_and_check_device_error()
+    assert torch.equal(small, full[:rows])
+    assert_close_bf16(small, oracle_gemm(a[:rows].cpu(), b[:len(counts)].cpu(),
+                                         off[:len(counts) + 1]))
