@@ -161,9 +161,12 @@ def gemm_cases(ref, out_dir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("LSEK_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("LSEK_REFERENCE"),
+                    help="checkout of the reference project (or set LSEK_REFERENCE)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref or set LSEK_REFERENCE to the reference checkout")
     ref = load_reference(args.ref)
     gating_cases(ref, args.out)
     adaptive_cases(ref, args.out)
