@@ -472,8 +472,34 @@ def decode_latency(layer, E, dev, peaks, reps=30):
         floor_us = floor_bytes / (peaks["hbm_gbs"] * 1e9) * 1e6
         out[str(t)] = {"us": ms * 1e3, "touched_experts": touched, "floor_us": floor_us,
                        "frac_of_floor": floor_us / (ms * 1e3)}
+        # The same call replayed from a CUDA graph (how a decode loop runs it):
+        # no host launch gaps between the layer's kernels.
+        try:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                layer(hidden, logits, out=y)
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                layer(hidden, logits, out=y)
+            gtimes = []
+            for _ in range(reps):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                graph.replay()
+                b.record()
+                torch.cuda.synchronize()
+                gtimes.append(a.elapsed_time(b))
+            del graph
+            gus = statistics.median(gtimes) * 1e3
+            out[str(t)].update({"us_graph": gus, "frac_of_floor_graph": floor_us / gus})
+        except RuntimeError as exc:
+            out[str(t)]["us_graph"] = None
+            out[str(t)]["graph_error"] = str(exc).splitlines()[0][:200]
     return {"workload": "cfg4: decode-shaped layer, T in {1, 8, 32, 64}, cfg1 weights resident "
-                        "(22.5 GB, larger than L2, so touched experts stream from HBM)",
+                        "(22.5 GB, larger than L2, so touched experts stream from HBM); "
+                        "us = eager call, us_graph = the call replayed from a CUDA graph",
             "by_tokens": out}
 
 

@@ -176,3 +176,37 @@ def test_bind_host_to_device():
             assert os.sched_getaffinity(0) == set(cores)
     finally:
         os.sched_setaffinity(0, before)
+
+
+@pytest.mark.parametrize("T", [1, 64, 300])
+def test_layer_replays_from_a_cuda_graph(T):
+    """The layer launches nothing that a CUDA graph cannot hold: captured once
+    (workspace and outputs preallocated), a replay on new inputs written into
+    the same buffers gives the bits of an eager call.  T=1 / 64 take the
+    decode and gathered paths, 300 the row copy."""
+    import layerstormexpertkernels_b200 as P
+    from layerstormexpertkernels_b200.synthetic import expert_weights, token_inputs
+    E, H, I = 32, 1024, 512
+    w_gu, w_down = expert_weights(E, H, I, device="cuda", seed_base=4000)
+    x0, x1 = token_inputs(T, E, H, seed=T), token_inputs(T, E, H, seed=T + 1)
+    layer = P.MoELayer(w_gu, w_down, x0.bias.cuda(), topk=8, n_group=8, topk_group=4,
+                       max_tokens=T)
+    hidden, logits = x0.hidden.cuda(), x0.logits.cuda()
+    out = torch.empty_like(hidden)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            layer(hidden, logits, out=out)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        layer(hidden, logits, out=out)
+    hidden.copy_(x1.hidden.cuda())
+    logits.copy_(x1.logits.cuda())
+    graph.replay()
+    torch.cuda.synchronize()
+    sync_and_check_device_error()
+    ref = layer(x1.hidden.cuda(), x1.logits.cuda())
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    del graph
