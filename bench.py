@@ -427,16 +427,19 @@ def swiglu_sweep(peaks, reps=20):
         g = torch.Generator(device=dev).manual_seed(n)
         x = torch.randn(n, 2 * INTER, generator=g, device=dev).to(torch.bfloat16)
         P.fused_swiglu(x)
-        times = []
+        torch.cuda.synchronize()
+        # All reps enqueued before one synchronize: the host runs ahead, so no
+        # launch gap of the host falls between an event and its kernel.
+        marks = []
         for _ in range(reps):
             flush()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             P.fused_swiglu(x)
             b.record()
-            torch.cuda.synchronize()
-            times.append(a.elapsed_time(b))
-        ms = statistics.median(times)
+            marks.append((a, b))
+        torch.cuda.synchronize()
+        ms = statistics.median(a.elapsed_time(b) for a, b in marks)
         gbs = n * 12288 / (ms * 1e-3) / 1e9
         out[str(n)] = {"us": ms * 1e3, "gbs": gbs, "frac_of_hbm": gbs / peaks["hbm_gbs"]}
     return {"workload": "cfg2: fused_swiglu [N, 4096] -> [N, 2048] bf16, L2 flushed per call",
