@@ -264,10 +264,23 @@ __global__ void __launch_bounds__(kThreads) copy_valid_rows_kernel(
   for (int j = 0; j < topk; ++j) any |= s_dest[j] < nv;
   if (!any) return;
   const uint4* srow = src + static_cast<int64_t>(t) * vec_per_row;
-  for (int64_t v = threadIdx.x; v < vec_per_row; v += kThreads) {
-    const uint4 r = ldg_nc_v4(srow + v);
-    for (int j = 0; j < topk; ++j)
-      if (s_dest[j] < nv) dst[static_cast<int64_t>(s_dest[j]) * vec_per_row + v] = r;
+  // Eight 16-byte loads in flight per thread before the stores.
+  for (int64_t v0 = threadIdx.x; v0 < vec_per_row; v0 += 8 * kThreads) {
+    uint4 r[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t v = v0 + u * kThreads;
+      if (v < vec_per_row) r[u] = ldg_nc_v4(srow + v);
+    }
+    for (int j = 0; j < topk; ++j) {
+      if (s_dest[j] >= nv) continue;
+      uint4* drow = dst + static_cast<int64_t>(s_dest[j]) * vec_per_row;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t v = v0 + u * kThreads;
+        if (v < vec_per_row) drow[v] = r[u];
+      }
+    }
   }
 }
 
