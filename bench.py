@@ -64,38 +64,82 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples every 200 ms while running."""
+    """SM clock and throttle-reason samples of one GPU while running: NVML
+    polled every 10 ms from a thread (a timed region of a few tens of
+    milliseconds still gets samples), else `nvidia-smi -lms 200`.  The GPU is
+    found by the PCI bus id of the torch device, so CUDA_VISIBLE_DEVICES
+    renumbering does not matter."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    # NVML clocks-event reason bits and the names the report uses.
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    SMI_REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu_index = gpu_index
-        self.rows = []
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.samples = []  # (sm_mhz, max_mhz, frozenset of reason names)
         self.proc = None
         self.thread = None
+        self.stop_flag = threading.Event()
+
+    def _bus_id(self):
+        import torch
+        p = torch.cuda.get_device_properties(self.device_index)
+        return f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(self._bus_id())
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # no NVML: nvidia-smi at its shortest interval
+            self._start_smi()
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+
+        def poll():
+            while not self.stop_flag.is_set():
+                try:
+                    sm = pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)
+                    bits = get_reasons(handle)
+                except Exception:
+                    break
+                self.samples.append((float(sm), float(max_mhz), frozenset(
+                    n for n, b in self.REASON_BITS.items() if bits & b)))
+                self.stop_flag.wait(0.01)
+            pynvml.nvmlShutdown()
+
+        self.thread = threading.Thread(target=poll, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
+    def _start_smi(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--id=" + self._bus_id(), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+
+        def read():
+            for line in self.proc.stdout:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 6 and parts[0].replace(".", "").isdigit():
+                    self.samples.append((float(parts[0]), float(parts[1]) if parts[1].replace(
+                        ".", "").isdigit() else 0.0, frozenset(
+                        n for n, v in zip(self.SMI_REASONS, parts[2:6]) if v.lower() == "active")))
+
+        self.thread = threading.Thread(target=read, daemon=True)
+        self.thread.start()
 
     def stop(self):
+        self.stop_flag.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -106,16 +150,14 @@ class ClockSampler:
             self.thread.join(timeout=5)
 
     def summary(self):
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        sm = [x[0] for x in self.samples]
+        mx = [x[1] for x in self.samples if x[1] > 0]
         reasons = set()
-        for r in self.rows:
-            for name, v in zip(self.REASONS, r[5:9]):
-                if v.lower() == "active":
-                    reasons.add(name)
+        for x in self.samples:
+            reasons |= x[2]
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+                "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
 def dist_env():

@@ -26,10 +26,7 @@ def test_roofline_picks_tensor_for_many_rows_per_expert():
 
 def test_clock_summary_flags_throttle_reasons():
     s = bench.ClockSampler(0)
-    s.rows = [["0", "1965", "1965", "900", "0x0", "Not Active", "Not Active", "Not Active",
-               "Active"],
-              ["0", "1800", "1965", "990", "0x4", "Not Active", "Not Active", "Not Active",
-               "Active"]]
+    s.samples = [(1965.0, 1965.0, frozenset({"sw_power_cap"})), (1800.0, 1965.0, frozenset())]
     out = s.summary()
     assert out["sm_mhz"] == (1965 + 1800) / 2 and out["sm_max_mhz"] == 1965
     assert out["reasons"] == ["sw_power_cap"] and out["samples"] == 2
