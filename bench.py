@@ -720,10 +720,10 @@ def run_ep(args):
 
     plan = 1 + route_launches(T * world) + 1
     permute = route_launches(recv_rows * TOPK) + 1
-    if peer:  # gating, plan, push, wait, permute, gate/up, scan, combine plan,
+    if peer:  # gating, plan, counts read, push, wait, permute, gate/up, scan, combine plan,
         # down+combine (fused) or push_chunks x (down GEMM, combine push), wait, scan, reduce
         down = 2 * layer.push_chunks if layer.combine == "push" else 1
-        launches = 1 + plan + 1 + 1 + permute + 1 + 1 + 1 + down + 1 + 1 + 1
+        launches = 1 + plan + 1 + 1 + 1 + permute + 1 + 1 + 1 + down + 1 + 1 + 1
     else:     # gating, plan, pack, permute, gate/up, down, scan, combine pack, scan, reduce
         launches = 1 + plan + 1 + permute + 2 + 2 + 1 + 1
     if rank == 0:
