@@ -25,6 +25,8 @@
 // particular single-precision exp implementation.
 #include <float.h>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace lsek {
@@ -179,15 +181,12 @@ __global__ void __launch_bounds__(256, 3) topk_gating_kernel(
     float my_w = 0.0f;
     int my_i = 0;
     for (int k = 0; k < topk; ++k) {
-      uint32_t kk = bk;
-      int ie = (bj >= 0) ? e0 + bj : 0x7fffffff;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const uint32_t ok = __shfl_xor_sync(kFull, kk, off);
-        const int oi = __shfl_xor_sync(kFull, ie, off);
-        if (ok > kk || (ok == kk && oi < ie)) { kk = ok; ie = oi; }
-      }
-      const int owner = ie / EPL;
+      // Warp arg-max: the highest key (one redux), and among the lanes that
+      // hold it the lowest one, whose experts have the lowest ids (each lane
+      // already keeps its lowest j on ties).
+      const uint32_t kmax = __reduce_max_sync(kFull, bk);
+      const int owner = __ffs(__ballot_sync(kFull, bk == kmax)) - 1;
+      const int ie = owner * EPL + __shfl_sync(kFull, bj, owner);
       float mine = 0.0f;
 #pragma unroll
       for (int j = 0; j < EPL; ++j)
@@ -233,8 +232,24 @@ cudaError_t launch_topk(float* w, int32_t* idx, const float* logits,
       (p.n_group > 1 && seg == 0)
           ? static_cast<size_t>(warps) * (p.num_experts + (p.num_experts >> 5) + 1) * sizeof(float)
           : 0;
+  // One wave of resident blocks at most (one warp per token, so a token's
+  // latency chain is the kernel's critical path: no warp takes two tokens
+  // while the SMs could hold more).
+  // (The register-path occupancy is cached: the query is a driver call.)
+  static std::atomic<int> cached_per_sm{0};
+  int per_sm = smem == 0 ? cached_per_sm.load(std::memory_order_relaxed) : 0;
+  if (per_sm == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, topk_gating_kernel<EPL>, threads,
+                                                      smem) != cudaSuccess ||
+        per_sm < 1) {
+      cudaGetLastError();  // a failed query must not read as a failed launch
+      per_sm = 1;
+    }
+    if (smem == 0) cached_per_sm.store(per_sm, std::memory_order_relaxed);
+  }
   const int blocks_needed = static_cast<int>(ceil_div(p.num_tokens, warps));
-  const int grid = blocks_needed < num_sms() * 3 ? blocks_needed : num_sms() * 3;
+  const int cap = num_sms() * per_sm;
+  const int grid = blocks_needed < cap ? blocks_needed : cap;
   topk_gating_kernel<EPL><<<grid, threads, smem, st>>>(
       w, idx, logits, bias, p.num_tokens, p.num_experts, p.topk,
       p.n_group > 1 ? p.n_group : 1, p.topk_group, p.routed_scaling_factor,
