@@ -86,6 +86,19 @@ def test_gating_ties_go_to_lower_id():
     assert idx[0].tolist() == [0, 1, 2, 3, 4, 5]
 
 
+def test_gating_ties_at_deepseek_shape():
+    # E=256, 8 groups / 4 kept, top-8 (the register path, eight experts per
+    # lane): equal scores pick the lowest groups, then the lowest ids.
+    logits = np.zeros((3, 256), np.float32)
+    logits[1, 200:] = 1.0          # one group's tail ahead, the rest tied
+    logits[2, ::3] = -1.0
+    c = dict(topk=8, n_group=8, topk_group=4, rsf=2.5, renorm=True, scoring="sigmoid")
+    w, idx = run_gating(logits, None, c)
+    ow, oidx = O.topk_gating(logits, None, 8, 8, 4, 2.5, True)
+    check_gating(w, idx, ow, oidx)
+    assert idx[0].tolist() == list(range(8))
+
+
 def test_gating_sqrtsoftplus_extremes():
     # tests/test_topk_gating.py:274-297: large / small logits stay finite.
     logits = np.zeros((8, 64), np.float32)
