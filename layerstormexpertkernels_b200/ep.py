@@ -1,5 +1,7 @@
 """Expert-parallel MoE layer: experts sharded over the ranks of a process
-group, tokens exchanged with two NCCL all-to-alls.
+group, tokens exchanged either with two NCCL all-to-alls or through peer
+memory over NVLink (`PeerDomain`: the dispatch and combine kernels store
+straight into the owner's buffers, epoch flags order them).
 
 Rank g of G owns experts [g*E/G, (g+1)*E/G).  Per layer:
 
@@ -7,14 +9,15 @@ Rank g of G owns experts [g*E/G, (g+1)*E/G).  Per layer:
   2. plan: a stable counting sort of (token, destination rank) pairs gives
      each destination's send rows in token order, and per destination the
      number of rows and of (token, slot) pairs it serves; the [G, 2] counts
-     go through one small all-to-all and one device->host copy (the only
-     host synchronisation of the layer);
+     are exchanged once and read by the host once (the only host
+     synchronisation of the layer);
   3. dispatch: each token row once per distinct owner rank, with per slot
      the expert's local index (-1 for other ranks' experts) and weight;
   4. expert side: permute the received rows by local expert (only own
      slots are copied), gate/up GEMM with fused SwiGLU, down GEMM, then the
      weighted per-slot pack bf16(w * y) in received-row and slot order;
-  5. combine: the packed slots go back with the reverse all-to-all;
+  5. combine: the packed slots go back (the reverse all-to-all, or a push
+     into the source rank's combine buffer);
   6. the source rank sums each token's slots in slot order in fp32 from 0
      and rounds once to bf16.
 
@@ -27,7 +30,7 @@ all-reduce of [T, topk, H] (tests/test_kernels.py:131-142, 187-200); only
 the rows that cross ranks travel here.
 
 Every data-path step is a CUDA kernel of liblsek.so (`DeviceSteps`); the
-collectives are torch.distributed all_to_all_single calls
+NCCL transport's collectives are torch.distributed all_to_all_single calls
 (`ProcessGroupExchange`).  Both can be replaced: the CPU tests inject a
 restatement of the kernels to check this module's exchange logic over gloo,
 and the one-GPU tests run G ranks as threads with an in-process exchange.
