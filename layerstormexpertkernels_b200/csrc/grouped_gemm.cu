@@ -992,6 +992,7 @@ lsek_status validate(const char* name, const void* D, const void* A, const void*
   LSEK_REQUIRE(K % 8 == 0, "%s: K must be a multiple of 8 (16-byte rows), got %d", name, K);
   LSEK_REQUIRE(n_out % 32 == 0, "%s: output width must be a multiple of 32, got %d", name, n_out);
   if (rows == 0 || n_out == 0) return LSEK_OK;  // nothing to compute (pointers may be NULL)
+  LSEK_REQUIRE(K > 0, "%s: K must be > 0 when there are rows to compute", name);
   LSEK_REQUIRE(offsets != nullptr, "%s: expert_offsets is NULL", name);
   LSEK_REQUIRE(D && A && B, "%s: NULL tensor pointer", name);
   LSEK_REQUIRE(reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(B) % 16 == 0 &&

@@ -123,6 +123,8 @@ def test_gemm_invalid(lib):
     assert lib.lsek_grouped_gemm_bf16(d, d, d, d, 2048, 8, 64, 64, None, z, None) == LSEK_ERR_UNSUPPORTED
     odd = ctypes.c_void_p(18)
     assert lib.lsek_grouped_gemm_bf16(d, odd, d, d, 4, 8, 64, 64, None, z, None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_grouped_gemm_bf16(d, d, d, d, 4, 8, 64, 0, None, z, None) == LSEK_ERR_INVALID_ARG  # K = 0
+    assert b"K must be > 0" in lib.lsek_last_error()
 
 
 def test_adaptive_invalid(lib):
