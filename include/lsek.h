@@ -373,7 +373,8 @@ LSEK_API lsek_status lsek_ep_dispatch_push(lsek_ep_domain* d, int32_t* send_ids,
  * stream (the copy engine serves those in order).  Used to read the
  * expert-parallel counts while the previous batch's output is being copied
  * out.  host_dst must be page-locked (cudaHostAlloc or cudaHostRegister);
- * the data is in place once the stream has passed this call. */
+ * the data is in place once the stream has passed this call.  No
+ * counterpart in the reference (its host reads go through torch copies). */
 LSEK_API lsek_status lsek_copy_to_mapped_host(void* host_dst, const void* dev_src, size_t bytes,
                                               void* stream);
 /* Waits on the stream until every rank has published `epoch` for the
