@@ -81,6 +81,26 @@ def test_permute_zero_tokens():
     assert p.shape == (0, 64) and off.shape == (17,) and int(off.abs().sum()) == 0
 
 
+@pytest.mark.parametrize("T", [4096, 8192])
+def test_permute_properties_full_size(T):
+    """BASELINE cfg1 / cfg3 token counts at the DeepSeek-V3 row width:
+    sorted, stable, inverse maps, offsets from counts, rows copied bitwise;
+    then the round trip through the weighted unpermute with power-of-two
+    weights summing to 1 (every fp32 partial sum exact) returns the tokens
+    bit for bit."""
+    from permute_props import check_permute_properties
+    k, E, H = 8, 256, 7168
+    idx = cases.permute_indices(T, k, E, 0.0, seed=T)
+    g = torch.Generator(device="cuda").manual_seed(T)
+    hidden = torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16)
+    p, off, s2d, perm = ek().moe_permute(hidden, idx.cuda(), E)
+    check_permute_properties(hidden, idx, E, p, off, s2d, perm)
+    w = torch.tensor([0.5, 0.25, 0.125, 0.0625, 0.03125, 0.015625, 0.0078125, 0.0078125],
+                     device="cuda").expand(T, k).contiguous()
+    back = ek().moe_unpermute(p, w, s2d, T, k)
+    assert torch.equal(back.view(torch.int16), hidden.view(torch.int16))
+
+
 def test_reference_roundtrip_case():
     # tests/test_kernels.py:58-88
     B, D, E, k = 128, 512, 32, 4
