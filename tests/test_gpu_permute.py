@@ -237,6 +237,18 @@ def test_swiglu_golden(golden_dir, name):
     assert (np.abs(got - ref) <= np.maximum(np.abs(ref) * 2.0 ** -7, 2.0 ** -100)).all()
 
 
+def test_swiglu_full_size_sweep_shape():
+    """BASELINE cfg2's largest call, [65536, 2*2048] bf16 ~ N(0,1): every output
+    within one bf16 ulp of silu(g)*u evaluated in float64 on the GPU."""
+    g = torch.Generator(device="cuda").manual_seed(65536)
+    x = torch.randn(65536, 4096, generator=g, device="cuda").to(torch.bfloat16)
+    out = ek().fused_swiglu(x)
+    gd, ud = x[:, :2048].double(), x[:, 2048:].double()
+    ref = gd / (1.0 + torch.exp(-gd)) * ud
+    tol = torch.clamp(ref.abs() * 2.0 ** -7, min=2.0 ** -100)
+    assert bool(((out.double() - ref).abs() <= tol).all())
+
+
 def test_swiglu_fp16():
     gate = rand_bf16((64, 256), seed=1, dtype=torch.float16)
     up = rand_bf16((64, 256), seed=2, dtype=torch.float16)
