@@ -210,8 +210,22 @@ def cpu_layer_sample(logits, bias, hidden_bf16_f32, n_experts_sample, seed=0):
     return est, desc
 
 
+def _synthetic_module():
+    """The seeded input generator, loaded by file path: it is pure torch, and
+    loading it this way keeps the CPU arm free of the package __init__ (which
+    needs the native extension), so `--impl reference` runs on a box where
+    the CUDA build is missing."""
+    import importlib.util
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "layerstormexpertkernels_b200",
+                        "synthetic.py")
+    spec = importlib.util.spec_from_file_location("_lsek_synthetic", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def cpu_inputs():
-    from layerstormexpertkernels_b200.synthetic import token_inputs
+    token_inputs = _synthetic_module().token_inputs
     x = token_inputs(T_TOKENS, EXPERTS, HIDDEN, seed=0)
     return x.logits.numpy(), x.bias.numpy(), x.hidden.float().numpy()
 

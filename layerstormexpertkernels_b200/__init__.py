@@ -10,7 +10,8 @@ reference) under the same names.  `import sm120_expert_kernels` gives the same
 module under the reference's name.
 
 There is no CPU fallback: importing fails when the native extension has not
-been built (python -m layerstormexpertkernels_b200.build).
+been built.  Build it with `python layerstormexpertkernels_b200/build.py`
+(run as a script: `python -m` would execute this file first).
 """
 from __future__ import annotations
 
@@ -26,7 +27,7 @@ try:
 except ImportError as exc:  # pragma: no cover - exercised only on broken installs
     raise ImportError(
         "layerstormexpertkernels_b200: the native extension is not built "
-        f"({exc}); run `python -m layerstormexpertkernels_b200.build`") from exc
+        f"({exc}); run `python layerstormexpertkernels_b200/build.py`") from exc
 
 from ._C import (  # noqa: E402,F401
     adaptive_gating,

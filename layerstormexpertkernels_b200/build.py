@@ -10,7 +10,13 @@
 Both land in this package directory so they travel with the source tree.
 A target is rebuilt only when one of its inputs is newer.
 
-    python -m layerstormexpertkernels_b200.build [--force] [--jobs N]
+    python layerstormexpertkernels_b200/build.py [--force] [--jobs N]
+
+This file imports nothing from its package, so it runs in a checkout that
+has no native extension yet.  Run it as a script (or load it by path, as
+__graft_entry__.build() does): `python -m layerstormexpertkernels_b200.build`
+executes the package __init__ first, and that refuses to load without the
+extension.
 """
 from __future__ import annotations
 

@@ -24,7 +24,7 @@ def declared_symbols():
 
 @pytest.fixture(scope="module")
 def lib():
-    assert os.path.exists(LIB), "liblsek.so not built (python -m layerstormexpertkernels_b200.build)"
+    assert os.path.exists(LIB), "liblsek.so not built (python layerstormexpertkernels_b200/build.py)"
     lib = ctypes.CDLL(LIB)
     lib.lsek_last_error.restype = ctypes.c_char_p
     lib.lsek_version.restype = ctypes.c_char_p
