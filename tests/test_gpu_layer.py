@@ -82,6 +82,116 @@ def test_layer_deepseek_shape_sampled(deepseek_weights, T, sample):
     assert_layer_close(out[torch.as_tensor(toks).cuda()], np.concatenate(refs))
 
 
+# Experts with crafted row counts at cfg1 and the GEMM tile class each one
+# exercises (tiles are 128 rows; consecutive m-tiles of an expert pair up;
+# an unpaired tile of <= 64 rows runs with swapped operands).
+TILE_CLASS_COUNTS = {
+    3: 1,       # one swapped tile, one valid row
+    9: 64,      # one swapped tile, full swap width
+    17: 65,     # one unswapped unpaired tile, 65 valid rows
+    30: 128,    # one full unpaired tile
+    33: 129,    # a paired unit whose second tile has one row
+    40: 256,    # a paired unit of two full tiles
+    47: 300,    # a paired unit + an unpaired swapped tail of 44 rows
+    55: 356,    # a paired unit + an unpaired unswapped tail of 100 rows
+    62: 1100,   # the heaviest expert: four paired units + an unpaired 76-row tail
+}
+# Partners for the probe tokens' remaining slots (groups 2 and 3), so the
+# oracle needs the weights of only these 17 experts.
+PROBE_MATES = (69, 78, 87, 95, 98, 107, 116, 125)
+
+
+def _tile_boundary_ranks(count):
+    ranks = {0, count - 1}
+    for b in (63, 64, 127, 128, 255, 256, 511, 512, 1023, 1024):
+        if b < count:
+            ranks.add(b)
+    return ranks
+
+
+def craft_tile_class_routing(T=4096, E=256, k=8, n_group=8, seed=11):
+    """Per-token expert sets for which the special experts receive exactly
+    TILE_CLASS_COUNTS rows, each token's experts lie in at most four of the
+    eight groups, and the tokens at every tile-boundary rank of a special
+    expert ("probes") take their other slots from PROBE_MATES.  A token's
+    rank inside an expert is its position in token order (the permute is a
+    stable sort of t * k + slot).  Returns (sets [T] of lists, probe tokens)."""
+    rng = np.random.default_rng(seed)
+    epg = E // n_group
+    special = list(TILE_CLASS_COUNTS)
+    excluded = set(special) | set(PROBE_MATES)
+    taken = {e: 0 for e in special}
+    ranks = {e: _tile_boundary_ranks(c) for e, c in TILE_CLASS_COUNTS.items()}
+    sets, probes = [], []
+    for t in range(T):
+        left = T - t
+        joined, probe = [], False
+        for e in rng.permutation(special):
+            need = TILE_CLASS_COUNTS[e] - taken[e]
+            if need > 0 and (need >= left or rng.random() < need / left):
+                assert len(joined) < k, "routing construction ran out of slots"
+                probe |= taken[e] in ranks[e]
+                taken[e] += 1
+                joined.append(int(e))
+        if probe:
+            fill = [m for m in PROBE_MATES][: k - len(joined)]
+        else:
+            groups = {e // epg for e in joined}
+            while len(groups) < 4:
+                groups.add(int(rng.integers(n_group)))
+            pool = [e for g in sorted(groups) for e in range(g * epg, (g + 1) * epg)
+                    if e not in excluded]
+            fill = [int(e) for e in rng.choice(pool, size=k - len(joined), replace=False)]
+        sets.append(joined + fill)
+        if probe:
+            probes.append(t)
+    assert all(taken[e] == c for e, c in TILE_CLASS_COUNTS.items())
+    return sets, probes
+
+
+def test_layer_cfg1_every_tile_class_vs_oracle(deepseek_weights):
+    """cfg1 layer (T=4096) on crafted logits: experts with 1, 64, 65, 128,
+    129, 256, 300, 356 and 1100 rows, so every GEMM tile class of both
+    projections occurs (swapped small tiles, unpaired tiles, paired units with
+    full and one-row second tiles, unpaired tails above and below the swap
+    width, the heaviest expert's tail).  The tokens sitting at every
+    tile-boundary row of those experts are checked in full against the oracle
+    (all 7168 columns cross every n-tile of the down projection)."""
+    from layerstormexpertkernels_b200.synthetic import token_inputs
+    w_gu, w_down = deepseek_weights
+    T, E, H, k = 4096, 256, 7168, 8
+    sets, probes = craft_tile_class_routing(T, E, k)
+    x = token_inputs(T, seed=4242)
+    rng = np.random.default_rng(5)
+    logits = (rng.standard_normal((T, E)) * 0.5 - 8.0).astype(np.float32)
+    for t, s in enumerate(sets):
+        logits[t, s] = (4.0 + 0.5 * rng.random(len(s))).astype(np.float32)
+    x.logits = torch.from_numpy(logits)
+    out, w, idx = run_layer(x, w_gu, w_down, 8, 8, 4)
+    ow, oidx = O.topk_gating(logits, x.bias.numpy(), 8, 8, 4, 2.5, True)
+    gidx = idx.cpu().numpy()
+    assert np.array_equal(gidx, oidx)
+    assert np.abs(w.cpu().numpy() - ow).max() <= 1e-6 * np.abs(ow).max()
+    assert all(set(oidx[t].tolist()) == set(s) for t, s in enumerate(sets))
+    counts = np.bincount(oidx.ravel(), minlength=E)
+    for e, c in TILE_CLASS_COUNTS.items():
+        assert counts[e] == c
+    assert counts.argmax() == 62
+    toks = np.array(probes)
+    hidden = x.hidden.float().numpy()
+    y = np.zeros((len(toks), k, H), np.float32)
+    for e in sorted(set(oidx[toks].ravel().tolist())):
+        rows = [(i, j) for i, t in enumerate(toks) for j in np.nonzero(oidx[t] == e)[0]]
+        ye = O.expert_ffn(hidden[[toks[i] for i, _ in rows]], w_gu[e].float().cpu().numpy(),
+                          w_down[e].float().cpu().numpy())
+        for r, (i, j) in enumerate(rows):
+            y[i, j] = ye[r]
+    refs = [O.bf16_from_bits(O.moe_unpermute(O.bf16_bits(y[i]), ow[t:t + 1],
+                                             np.arange(k, dtype=np.int32), 1, k))
+            for i, t in enumerate(toks)]
+    assert_layer_close(out[torch.as_tensor(toks).cuda()], np.concatenate(refs))
+
+
 def test_layer_class_reuses_workspace(deepseek_weights):
     import layerstormexpertkernels_b200 as P
     from layerstormexpertkernels_b200.synthetic import token_inputs

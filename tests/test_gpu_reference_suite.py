@@ -1,0 +1,77 @@
+"""The reference's own GPU test files, run unchanged against this build.
+
+Callers of kkontosis/LayerStoRmExpertKernels import the extension as
+`import sm120_expert_kernels as EK` (tests/test_kernels.py:21 of the
+reference).  This test runs the reference's tests/test_kernels.py,
+tests/test_topk_gating.py and tests/test_fused_swiglu.py as they are, in a
+child pytest whose PYTHONPATH holds only this repository, so the module they
+import is this repository's sm120_expert_kernels.py (checked first).  Their
+CPU reference functions come from the reference's own
+tests/test_reference.py next to them.
+
+The reference checkout is not part of this repository.  The test finds its
+tests/ directory through $LSEK_REFERENCE_TESTS, else under baseline/_ref/tests
+(the git-ignored place for the reference's own code), and skips with that
+reason when neither holds the files.
+"""
+from __future__ import annotations
+
+import os
+import re
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_FILES = ("test_kernels.py", "test_topk_gating.py", "test_fused_swiglu.py")
+NEEDED = REF_FILES + ("test_reference.py", "__init__.py")
+
+
+def _reference_tests_dir() -> str | None:
+    candidates = [os.environ.get("LSEK_REFERENCE_TESTS", ""),
+                  os.path.join(ROOT, "baseline", "_ref", "tests")]
+    for c in candidates:
+        if c and all(os.path.isfile(os.path.join(c, f)) for f in NEEDED):
+            return os.path.abspath(c)
+    return None
+
+
+def _child_env() -> dict:
+    env = dict(os.environ)
+    env["PYTHONPATH"] = ROOT
+    return env
+
+
+@pytest.fixture(scope="module")
+def ref_tests():
+    d = _reference_tests_dir()
+    if d is None:
+        pytest.skip("the reference's tests/ directory is not on this machine: set "
+                    "LSEK_REFERENCE_TESTS or place it at baseline/_ref/tests")
+    parent = os.path.dirname(d)
+    probe = subprocess.run(
+        [sys.executable, "-c",
+         "import sm120_expert_kernels as EK, layerstormexpertkernels_b200 as P; "
+         "print(EK.__file__); print(EK.topk_gating is P.topk_gating)"],
+        cwd=parent, env=_child_env(), capture_output=True, text=True, timeout=300)
+    assert probe.returncode == 0, probe.stdout + probe.stderr
+    lines = probe.stdout.split()
+    assert lines[0] == os.path.join(ROOT, "sm120_expert_kernels.py"), probe.stdout
+    assert lines[1] == "True"
+    return d
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", REF_FILES)
+def test_reference_gpu_file_passes_unchanged(ref_tests, name):
+    parent = os.path.dirname(ref_tests)
+    out = subprocess.run(
+        [sys.executable, "-m", "pytest", "-q", "-rs", "-p", "no:cacheprovider", "--rootdir", parent,
+         os.path.join(ref_tests, name)],
+        cwd=parent, env=_child_env(), capture_output=True, text=True, timeout=1200)
+    tail = out.stdout[-6000:] + out.stderr[-3000:]
+    assert out.returncode == 0, tail
+    summary = out.stdout.strip().splitlines()[-1]
+    assert re.search(r"\d+ passed", summary), tail
+    assert "skipped" not in summary and "failed" not in summary and "error" not in summary, tail
