@@ -171,11 +171,31 @@ def dist_env():
 # CPU baseline: the oracle port of the reference's torch path
 # ---------------------------------------------------------------------------
 
-def cpu_layer_sample(logits, bias, hidden_bf16_f32, n_experts_sample, seed=0):
+# Both CPU legs (the reference arm and the cpu_baseline of our arm) time the
+# expert FFN on the same experts: CPU_SAMPLE_EXPERTS experts drawn with
+# CPU_SAMPLE_SEED from the non-empty ones.
+CPU_SAMPLE_EXPERTS = 4
+CPU_SAMPLE_SEED = 0
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_layer_sample(logits, bias, hidden_bf16_f32, n_experts_sample=CPU_SAMPLE_EXPERTS,
+                     seed=CPU_SAMPLE_SEED):
     """Times the CPU restatement of the layer on a bounded sample: gating,
     permute and unpermute over all tokens, the expert FFN on the rows of
-    `n_experts_sample` experts; returns (estimated seconds for the full
-    layer, description)."""
+    `n_experts_sample` experts, scaled by rows to all experts.  Returns a
+    dict: est_s (estimated seconds for the full layer), the measured parts
+    and the sample's size."""
     from oracle import moe_oracle as O
     t0 = time.perf_counter()
     w, idx = O.topk_gating(logits, bias, TOPK, N_GROUP, TOPK_GROUP, RSF, True)
@@ -184,7 +204,8 @@ def cpu_layer_sample(logits, bias, hidden_bf16_f32, n_experts_sample, seed=0):
     t2 = time.perf_counter()
     rng = np.random.default_rng(seed)
     counts = np.diff(offsets)
-    experts = rng.choice(np.nonzero(counts)[0], size=n_experts_sample, replace=False)
+    experts = sorted(int(e) for e in rng.choice(np.nonzero(counts)[0], size=n_experts_sample,
+                                                replace=False))
     y = np.zeros(permuted.shape, dtype=np.uint16)
     ffn = 0.0
     rows = 0
@@ -203,11 +224,24 @@ def cpu_layer_sample(logits, bias, hidden_bf16_f32, n_experts_sample, seed=0):
     O.moe_unpermute(y, w, s2d, idx.shape[0], TOPK)
     t4 = time.perf_counter()
     total_rows = int(offsets[-1])
-    est = (t1 - t0) + (t2 - t1) + ffn * total_rows / max(rows, 1) + (t4 - t3)
+    ffn_est = ffn * total_rows / max(rows, 1)
+    est = (t1 - t0) + (t2 - t1) + ffn_est + (t4 - t3)
     desc = (f"oracle port on the host: gating, permute and unpermute over all {idx.shape[0]} "
-            f"tokens; expert FFN (fp32 GEMMs, as ref_grouped_gemm) timed on {rows} rows of {n_experts_sample} experts "
-            f"and scaled to all {total_rows} rows")
-    return est, desc
+            f"tokens; expert FFN (fp32 GEMMs, as ref_grouped_gemm) timed on {rows} rows of "
+            f"experts {experts} and scaled to all {total_rows} rows")
+    return {"est_s": est, "desc": desc, "sample_experts": experts, "sample_rows": rows,
+            "total_rows": total_rows, "gating_s": t1 - t0, "permute_s": t2 - t1,
+            "ffn_sample_s": ffn, "ffn_scaled_s": ffn_est, "unpermute_s": t4 - t3}
+
+
+def cpu_baseline_record(r, cores, value):
+    return {"value": value, "unit": UNIT, "cores": cores, "cpu_model": cpu_model(),
+            "kind": "port", "sample": r["desc"],
+            "sample_experts": r["sample_experts"], "sample_rows": r["sample_rows"],
+            "total_rows": r["total_rows"],
+            "measured_s": {k: round(r[k], 6) for k in ("gating_s", "permute_s", "ffn_sample_s",
+                                                      "unpermute_s")},
+            "ffn_scaled_s": round(r["ffn_scaled_s"], 6)}
 
 
 def _synthetic_module():
@@ -239,11 +273,11 @@ def run_reference(args):
     torch.set_num_threads(cores)
     logits, bias, hidden = cpu_inputs()
     per_step = []
-    desc = ""
+    last = None
     for i in range(args.warmup + args.steps):
-        est, desc = cpu_layer_sample(logits, bias, hidden, n_experts_sample=2, seed=i)
+        last = cpu_layer_sample(logits, bias, hidden)
         if i >= args.warmup:
-            per_step.append(est)
+            per_step.append(last["est_s"])
     sec = statistics.mean(per_step)
     value = T_TOKENS / sec
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
@@ -251,8 +285,7 @@ def run_reference(args):
             "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "tokens": T_TOKENS, "parallelism": "cpu"},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": desc},
+            "cpu_baseline": cpu_baseline_record(last, cores, value),
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -452,9 +485,8 @@ def run_ours(args):
         cores = len(os.sched_getaffinity(0))
         _t.set_num_threads(cores)
         logits_np, bias_np, hidden_np = cpu_inputs()
-        est, desc = cpu_layer_sample(logits_np, bias_np, hidden_np, n_experts_sample=4)
-        line["cpu_baseline"] = {"value": T_TOKENS / est, "unit": UNIT, "cores": cores,
-                                "kind": "port", "sample": desc}
+        r = cpu_layer_sample(logits_np, bias_np, hidden_np)
+        line["cpu_baseline"] = cpu_baseline_record(r, cores, T_TOKENS / r["est_s"])
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
