@@ -136,6 +136,20 @@ LSEK_API lsek_status lsek_moe_permute(void* permuted_input, int32_t* expert_offs
                              void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* The routing half of lsek_moe_permute alone: expert_offsets [E+1],
+ * src_to_dest_map [T*topk] and permuted_idx [T*topk], identical to what
+ * lsek_moe_permute writes for the same topk_indices (same stable order, same
+ * sentinel handling), with no row copy and no workspace, in one launch.  For
+ * callers that gather the token rows themselves (the layer forward folds the
+ * gather into its GEMM or into its own copy).  E <= 1023.  Corresponds to
+ * steps 1-3 of launch_moe_permute (remap, CUB sort, offsets;
+ * smxx/permute/moe_permute.cu:47-92,553-575) without step 4
+ * (expand_input_rows). */
+LSEK_API lsek_status lsek_moe_route(int32_t* expert_offsets, int32_t* src_to_dest_map,
+                           int32_t* permuted_idx, const int32_t* topk_indices,
+                           int32_t num_tokens, int32_t topk, int32_t num_experts,
+                           void* stream);
+
 /* Size of the fixed device buffer behind lsek_moe_permute_noalloc (1 MiB). */
 #define LSEK_NOALLOC_PERMUTE_SCRATCH_BYTES (1u << 20)
 

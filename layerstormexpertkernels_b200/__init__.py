@@ -40,6 +40,7 @@ from ._C import (  # noqa: E402,F401
     moe_layer_forward_out,
     moe_layer_workspace_size,
     moe_permute,
+    moe_route,
     moe_unpermute,
     moe_unpermute_bf16_perslot,
     moe_unpermute_fp32,
@@ -53,7 +54,7 @@ __all__ = [
     "adaptive_gating", "device_error", "fused_swiglu", "grouped_gemm_bf16",
     "grouped_gemm_swiglu_bf16", "moe_combine_reduce_slots_bf16_to_bf16",
     "moe_combine_reduce_slots_fp32_to_bf16", "moe_layer_forward", "moe_layer_forward_out",
-    "moe_layer_workspace_size", "moe_permute", "moe_unpermute", "moe_unpermute_bf16_perslot",
+    "moe_layer_workspace_size", "moe_permute", "moe_route", "moe_unpermute", "moe_unpermute_bf16_perslot",
     "moe_unpermute_fp32", "topk_gating", "version", "MoELayer", "HostPipeline", "StageEvents", "bind_host_to_device",
     "STAGES",
     "LIBRARY_PATH",

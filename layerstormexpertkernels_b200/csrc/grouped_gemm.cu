@@ -44,14 +44,19 @@
 //               global, then release the accumulator; a single unit's
 //               epilogue overlaps the next unit's main loop thanks to the
 //               second accumulator (a paired unit waits for both).
-// Small unpaired tiles (at most kSwapMaxRows valid rows: experts of at most
-// 64 rows, the last tile of an expert with an odd tile count, every tile at
-// decode sizes) swap the operands: the two weight boxes become the MMA's M
-// side (2 x M=128) and the tile's r token rows its N side (N = r rounded up
-// to 16), so the tensor-core work scales with r instead of a full 128-row
-// tile.  The epilogue of such a tile reads
-// the transposed accumulator (TMEM lane = output column, TMEM column =
-// token).  The same products are summed in the same k order either way.
+// Small tiles (at most kSwapMaxRows valid rows: experts of at most 64 rows,
+// the last tile of an expert, whether it runs alone or as the second tile of
+// a paired unit, every tile at decode sizes) swap the operands: the two
+// weight boxes become the MMA's M side (2 x M=128) and the tile's r token
+// rows its N side (N = r rounded up to 16), so the tensor-core work scales
+// with r instead of a full 128-row tile.  At DeepSeek-V3 shape most paired
+// units are a full tile plus a few rows, and with the second tile swapped
+// the MMA holds each weight stage about half as long, so more of the ring
+// stays in flight.  Such a tile's A rows arrive as r/16 boxes of 16 rows
+// (a second tensor map) instead of one 128-row box.  The epilogue of a
+// swapped tile reads the transposed accumulator (TMEM lane = output column,
+// TMEM column = token).  The same products are summed in the same k order
+// either way.
 // COMBINE mode (the expert-parallel down projection) ends each output row
 // in the combine instead of D: row p becomes bf16(w[p] * bf16(acc)) stored at
 // row dst_row[p] of rank dst_rank[p]'s combine buffer (peer memory over
@@ -100,6 +105,7 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxExperts = 1024;
 constexpr int kUnitQ = 4;                      // unit ids in flight between warps
 constexpr int kSwapMaxRows = 64;               // tiles this small use swapped operands
+constexpr int kA16Bytes = 16 * kBK * 2;        // one 16-row A box (2 KB)
 
 // Pipeline geometry.  Each k-block of a unit is one stage: its A box (token
 // rows; two A boxes for a paired unit) followed by two 128-row weight boxes.
@@ -432,7 +438,8 @@ struct RingPos {
 template <int MODE, class G>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                        const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ Params p) {
+                        const __grid_constant__ CUtensorMap tmap_b,
+                        const __grid_constant__ CUtensorMap tmap_a16, const __grid_constant__ Params p) {
   constexpr bool SWIGLU = MODE == kModeSwiglu;
   constexpr bool COMBINE = MODE == kModeCombine;
   using Smem = SmemT<G>;
@@ -496,6 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a16)) : "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -564,6 +572,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Unit u = decode_unit(s, E, unit, pairs);
         const int row0 = s.offs[u.e] + u.t0 * kBM;
         const int brow = u.e * p.b_rows + u.n * p.b_tile_rows;
+        // A tile that runs with swapped operands needs only its rows rounded
+        // up to 16: it is loaded as that many 16-row boxes instead of one
+        // 128-row box (the stage keeps the full box's ring space).  Tiled A
+        // only; the first tile of a paired unit is always a full one.
+        const int rows_t0 = tile_rows(s, u.e, u.t0);
+        const int rows_t1 = u.pair ? tile_rows(s, u.e, u.t0 + 1) : 0;
+        const int n16_t0 = (!G::kSmallOnly && !u.pair && rows_t0 <= kSwapMaxRows && p.gather_idx == nullptr)
+                               ? (rows_t0 + 15) >> 4 : 0;
+        const int n16_t1 = (u.pair && rows_t1 <= kSwapMaxRows) ? (rows_t1 + 15) >> 4 : 0;
         // Gathered A: the MMA reads 128 rows (or, for a swapped small tile,
         // its rows rounded up to 16); rows past the expert repeat its first
         // row (their results are discarded).
@@ -574,10 +591,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int r = 0; r < nload; ++r)
             s.arow[r] = __ldg(p.gather_idx + row0 + (r < valid ? r : 0)) / p.gather_k;
         }
-        const uint32_t a_bytes =
-            p.gather_idx != nullptr ? static_cast<uint32_t>(nload * kBK * 2) : G::kABytes;
+        const uint32_t a_bytes = p.gather_idx != nullptr ? static_cast<uint32_t>(nload * kBK * 2)
+                                 : n16_t0 > 0           ? static_cast<uint32_t>(n16_t0 * kA16Bytes)
+                                                        : G::kABytes;
+        const uint32_t a1_bytes = !u.pair ? 0u
+                                  : n16_t1 > 0 ? static_cast<uint32_t>(n16_t1 * kA16Bytes)
+                                               : G::kABytes;
         const uint32_t stage_bytes = u.pair ? G::kPairStageBytes : G::kStageBytes;
-        const uint32_t tx = a_bytes + (u.pair ? G::kABytes : 0u) + 2u * kBoxBytes;
+        const uint32_t tx = a_bytes + a1_bytes + 2u * kBoxBytes;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!reserve(stage_bytes, tx)) {
             ok = false;
@@ -591,10 +612,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int r = 0; r < nload; r += 4)
               tma_gather4(a0 + r * kBK * 2, &tmap_a, full, kb * kBK, s.arow[r], s.arow[r + 1],
                           s.arow[r + 2], s.arow[r + 3], pol_a);
+          } else if (n16_t0 > 0) {
+            for (int b = 0; b < n16_t0; ++b)
+              tma_load_2d(a0 + b * kA16Bytes, &tmap_a16, full, kb * kBK, row0 + 16 * b, pol_a);
           } else {
             tma_load_2d(a0, &tmap_a, full, kb * kBK, row0, pol_a);
           }
-          if (u.pair) tma_load_2d(s.ring + oa1, &tmap_a, full, kb * kBK, row0 + kBM, pol_a);
+          if (u.pair) {
+            if (n16_t1 > 0) {
+              for (int b = 0; b < n16_t1; ++b)
+                tma_load_2d(s.ring + oa1 + b * kA16Bytes, &tmap_a16, full, kb * kBK,
+                            row0 + kBM + 16 * b, pol_a);
+            } else {
+              tma_load_2d(s.ring + oa1, &tmap_a, full, kb * kBK, row0 + kBM, pol_a);
+            }
+          }
           tma_load_2d(s.ring + ob0, &tmap_b, full, kb * kBK, brow, pol_w);
           tma_load_2d(s.ring + ob0 + kBoxBytes, &tmap_b, full, kb * kBK, brow + p.b_second, pol_w);
           pos.advance(stage_bytes);
@@ -629,6 +661,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool swapped = !u.pair && (G::kSmallOnly || rows_here <= kSwapMaxRows);
         const int nn = (rows_here + 15) & ~15;
         const uint32_t sw_idesc = swap_idesc(nn);
+        // A pair's second tile (the expert's last) with few rows also swaps.
+        const int rows1 = u.pair ? tile_rows(s, u.e, u.t0 + 1) : 0;
+        const bool swapped1 = u.pair && rows1 <= kSwapMaxRows;
+        const int nn1 = (rows1 + 15) & ~15;
+        const uint32_t sw_idesc1 = swap_idesc(nn1);
         const int acc0 = static_cast<int>(ac & 1u);
         const int acc1 = static_cast<int>((ac + 1) & 1u);
         if (!mbar_wait(&s.acc_empty_bar[acc0], ((ac >> 1) & 1u) ^ 1u, abort, kDevErrGemmMmaWait,
@@ -672,7 +709,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < kBK / 16; ++kk)
               umma_bf16(d0, smem_desc_sw128(a0_addr + kk * 32), smem_desc_sw128(b0_addr + kk * 32),
                         kIdesc, (kb | kk) != 0 ? 1u : 0u);
-            if (u.pair) {
+            if (swapped1) {
+#pragma unroll
+              for (int kk = 0; kk < kBK / 16; ++kk) {
+                const uint64_t tok = smem_desc_sw128(a1_addr + kk * 32);
+                const uint32_t acc_in = (kb | kk) != 0 ? 1u : 0u;
+                umma_bf16(d1, smem_desc_sw128(b0_addr + kk * 32), tok, sw_idesc1, acc_in);
+                umma_bf16(d1 + static_cast<uint32_t>(nn1), smem_desc_sw128(b1_addr + kk * 32), tok,
+                          sw_idesc1, acc_in);
+              }
+            } else if (u.pair) {
 #pragma unroll
               for (int kk = 0; kk < kBK / 16; ++kk)
                 umma_bf16(d1, smem_desc_sw128(a1_addr + kk * 32),
@@ -724,7 +770,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const int m = u.t0 + ti;
         const int rows_here = tile_rows(s, e, m);
-        const bool swapped = !u.pair && (G::kSmallOnly || rows_here <= kSwapMaxRows);
+        const bool swapped = G::kSmallOnly || rows_here <= kSwapMaxRows;
         const int row0 = s.offs[e] + m * kBM;
         const int r = row0 + q * 32 + lane;
         const bool valid = r < s.offs[e + 1];
@@ -935,6 +981,12 @@ lsek_status launch_geom(void* D, const void* A, const void* B, const int32_t* of
   if (s != LSEK_OK) return s;
   s = make_map(&mb, B, static_cast<uint64_t>(K), static_cast<uint64_t>(E) * b_rows);
   if (s != LSEK_OK) return s;
+  // 16-row boxes for tiles that run with swapped operands (tiled A only).
+  CUtensorMap ma16 = ma;
+  if (gather.idx == nullptr && !G::kSmallOnly) {
+    s = make_map(&ma16, A, static_cast<uint64_t>(K), static_cast<uint64_t>(rows), 16u);
+    if (s != LSEK_OK) return s;
+  }
   Params p;
   if (combine != nullptr) p = *combine;
   p.offsets = offsets;
@@ -964,7 +1016,7 @@ lsek_status launch_geom(void* D, const void* A, const void* B, const int32_t* of
   const int64_t max_units = (ceil_div(rows, kBM) + E) * static_cast<int64_t>(p.n_tiles);
   const int grid = static_cast<int>(max_units < num_sms() ? max_units : num_sms());
   if (MODE == kModeCombine) LSEK_CUDA_TRY(cudaMemsetAsync(p.done, 0, sizeof(uint32_t), st));
-  grouped_gemm_kernel<MODE, G><<<grid, kThreads, smem_bytes<G>(), st>>>(ma, mb, p);
+  grouped_gemm_kernel<MODE, G><<<grid, kThreads, smem_bytes<G>(), st>>>(ma, mb, ma16, p);
   return check_launch(SWIGLU ? "grouped_gemm_swiglu_bf16"
                              : (MODE == kModeCombine ? "ep_down_gemm_combine" : "grouped_gemm_bf16"));
 }

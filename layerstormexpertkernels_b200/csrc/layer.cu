@@ -16,6 +16,8 @@ namespace lsek {
 size_t permute_workspace_bytes(int64_t n_keys, int num_experts);
 lsek_status launch_route(const int32_t* idx, int64_t n, int E, int32_t* offsets, int32_t* s2d,
                          int32_t* perm, void* ws, cudaStream_t st);
+lsek_status launch_route_by_expert(const int32_t* idx, int64_t n, int E, int32_t* offsets,
+                                   int32_t* s2d, int32_t* perm, cudaStream_t st);
 lsek_status grouped_gemm_plain(void* D, const void* A, const void* B, const int32_t* offsets,
                                int E, int rows, int N, int K, int32_t* counter, cudaStream_t st,
                                int max_rows_per_expert);
@@ -114,7 +116,7 @@ extern "C" lsek_status lsek_moe_layer_forward(
   if ((s = mark(0)) != LSEK_OK) return s;
   if ((s = lsek_topk_gating(w, idx, logits, bias, gp, stream)) != LSEK_OK) return s;
   if ((s = mark(1)) != LSEK_OK) return s;
-  if ((s = launch_route(idx, n, E, offs, s2d, perm, ws + l.route, st)) != LSEK_OK) return s;
+  if ((s = launch_route_by_expert(idx, n, E, offs, s2d, perm, st)) != LSEK_OK) return s;
   // The top-k experts of a token are distinct, so no expert gets more than T
   // rows.  Up to kGatherMaxTokens tokens every tile is a small one, and the
   // permute is folded into the gate/up GEMM's A load (a tile's few token rows

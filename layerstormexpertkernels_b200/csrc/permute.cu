@@ -271,6 +271,170 @@ __global__ void __launch_bounds__(kRouteThreads) route_rank_kernel(
   rank_keys<kChunkKeyPerLane>(key, cnt, rb, lane, E, nbits, s2d, perm);
 }
 
+// ---- route by expert ---------------------------------------------------------------
+//
+// One CTA per kRbeExperts consecutive experts (the sentinel bin E is the last
+// "expert"), no workspace and one launch.  Every CTA reads all n keys (they
+// were just written by the gating kernel, so they come from L2).  For its
+// experts e the CTA needs
+//   offsets[e] = #{keys < e}                      (a block sum of counts)
+//   dest(pos)  = offsets[e] + #{keys == e at positions < pos}.
+// In a round, warp w covers 32 * kRbeKeys consecutive positions; lane l loads
+// 16-byte vectors at chunk c = 0..kRbeVecs-1, positions c*128 + 4l .. +3 (one
+// 512-byte coalesced load per warp and chunk), so inside a warp the position
+// order is chunk, then lane, then vector element.  A key's rank is: matches
+// of the earlier warps (a scan of per-warp counts through shared memory) +
+// matches in the warp's earlier chunks + matches of lower lanes in its chunk
+// (ballots) + its own earlier matches.  That is the order of a stable sort by
+// expert, the order of torch.argsort(stable=True)
+// (tests/test_reference.py:534-558) and of the reference's CUB radix sort
+// (smxx/permute/moe_permute.cu:553-563).  With more than one round the
+// totals are counted in a first pass.
+constexpr int kRbeVecs = 8;                   // 16-byte key vectors per lane per round
+constexpr int kRbeKeys = 4 * kRbeVecs;        // keys per lane per round
+constexpr int kRbeWarpKeys = 32 * kRbeKeys;   // keys per warp per round
+constexpr int kRbeExperts = 2;                // experts per CTA
+constexpr int kRbePad = 0x7fffffff;           // past the end: below no expert, equal to none
+
+// v[4c + q] = key at position wb + 128c + 4*lane + q (kRbePad past n).
+__device__ __forceinline__ void rbe_load(int (&v)[kRbeKeys], const int32_t* __restrict__ idx,
+                                         int64_t wb, int lane, int64_t n, int E, bool vec_ok) {
+#pragma unroll
+  for (int c = 0; c < kRbeVecs; ++c) {
+    const int64_t p = wb + 128 * c + 4 * lane;
+    if (vec_ok && p + 4 <= n) {
+      const int4 q = __ldg(reinterpret_cast<const int4*>(idx + p));
+      v[4 * c] = clamp_key(q.x, E);
+      v[4 * c + 1] = clamp_key(q.y, E);
+      v[4 * c + 2] = clamp_key(q.z, E);
+      v[4 * c + 3] = clamp_key(q.w, E);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[4 * c + q] = p + q < n ? clamp_key(__ldg(idx + p + q), E) : kRbePad;
+    }
+  }
+}
+
+// Sum over the block of per-warp values published in s[0..nw) (after a
+// barrier); every thread gets the total, lane-parallel.
+__device__ __forceinline__ int rbe_sum_warps(const int* s, int nw, int lane) {
+  return __reduce_add_sync(kFull, lane < nw ? s[lane] : 0);
+}
+
+__global__ void __launch_bounds__(1024) route_by_expert_kernel(
+    const int32_t* __restrict__ idx, int64_t n, int E, int vec_ok, int32_t* __restrict__ offsets,
+    int32_t* __restrict__ s2d, int32_t* __restrict__ perm) {
+  __shared__ int s_cnt[kRbeExperts + 1][32];  // per warp: matches of each expert; keys below e0
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = blockDim.x >> 5;
+  const int e0 = blockIdx.x * kRbeExperts;
+  const int64_t per_round = static_cast<int64_t>(nw) * kRbeWarpKeys;
+  const int64_t rounds = (n + per_round - 1) / per_round;
+  int off[kRbeExperts];
+  int base[kRbeExperts];
+#pragma unroll
+  for (int j = 0; j < kRbeExperts; ++j) base[j] = 0;
+  if (rounds > 1) {
+    int lt = 0, eq[kRbeExperts] = {};
+    for (int64_t r = 0; r < rounds; ++r) {
+      int v[kRbeKeys];
+      rbe_load(v, idx, r * per_round + static_cast<int64_t>(warp) * kRbeWarpKeys, lane, n, E, vec_ok);
+#pragma unroll
+      for (int i = 0; i < kRbeKeys; ++i) {
+        lt += v[i] < e0;
+#pragma unroll
+        for (int j = 0; j < kRbeExperts; ++j) eq[j] += v[i] == e0 + j;
+      }
+    }
+    lt = __reduce_add_sync(kFull, lt);
+#pragma unroll
+    for (int j = 0; j < kRbeExperts; ++j) eq[j] = __reduce_add_sync(kFull, eq[j]);
+    if (lane == 0) {
+      s_cnt[kRbeExperts][warp] = lt;
+#pragma unroll
+      for (int j = 0; j < kRbeExperts; ++j) s_cnt[j][warp] = eq[j];
+    }
+    __syncthreads();
+    off[0] = rbe_sum_warps(s_cnt[kRbeExperts], nw, lane);
+#pragma unroll
+    for (int j = 1; j < kRbeExperts; ++j) off[j] = off[j - 1] + rbe_sum_warps(s_cnt[j - 1], nw, lane);
+    __syncthreads();
+  }
+  const unsigned lanes_below = lanemask_lt();
+  for (int64_t r = 0; r < rounds; ++r) {
+    const int64_t wb = r * per_round + static_cast<int64_t>(warp) * kRbeWarpKeys;
+    int v[kRbeKeys];
+    rbe_load(v, idx, wb, lane, n, E, vec_ok);
+    int lt = 0;
+    uint32_t m[kRbeExperts] = {};
+#pragma unroll
+    for (int i = 0; i < kRbeKeys; ++i) {
+      lt += v[i] < e0;
+#pragma unroll
+      for (int j = 0; j < kRbeExperts; ++j) m[j] |= static_cast<uint32_t>(v[i] == e0 + j) << i;
+    }
+    lt = __reduce_add_sync(kFull, lt);
+    int cw[kRbeExperts];
+#pragma unroll
+    for (int j = 0; j < kRbeExperts; ++j) cw[j] = __reduce_add_sync(kFull, __popc(m[j]));
+    if (lane == 0) {
+      s_cnt[kRbeExperts][warp] = lt;
+#pragma unroll
+      for (int j = 0; j < kRbeExperts; ++j) s_cnt[j][warp] = cw[j];
+    }
+    __syncthreads();
+    // Lane l holds warp l's count: an inclusive scan over lanes gives every
+    // warp its prefix and the block total.
+    int wpre[kRbeExperts], tot[kRbeExperts];
+#pragma unroll
+    for (int j = 0; j < kRbeExperts; ++j) {
+      const int c = lane < nw ? s_cnt[j][lane] : 0;
+      int inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(kFull, inc, o);
+        if (lane >= o) inc += t;
+      }
+      wpre[j] = __shfl_sync(kFull, inc - c, warp);
+      tot[j] = __shfl_sync(kFull, inc, 31);
+    }
+    if (rounds == 1) {
+      off[0] = rbe_sum_warps(s_cnt[kRbeExperts], nw, lane);
+#pragma unroll
+      for (int j = 1; j < kRbeExperts; ++j) off[j] = off[j - 1] + tot[j - 1];
+    }
+    __syncthreads();  // s_cnt is rewritten by the next round
+#pragma unroll
+    for (int j = 0; j < kRbeExperts; ++j) {
+      int d = off[j] + base[j] + wpre[j];
+#pragma unroll
+      for (int c = 0; c < kRbeVecs; ++c) {
+        uint32_t own = (m[j] >> (4 * c)) & 0xFu;
+        if (!__any_sync(kFull, own != 0u)) continue;
+        const uint32_t b0 = __ballot_sync(kFull, own & 1u), b1 = __ballot_sync(kFull, own & 2u);
+        const uint32_t b2 = __ballot_sync(kFull, own & 4u), b3 = __ballot_sync(kFull, own & 8u);
+        int dd = d + __popc(b0 & lanes_below) + __popc(b1 & lanes_below) +
+                 __popc(b2 & lanes_below) + __popc(b3 & lanes_below);
+        while (own != 0u) {
+          const int q = __ffs(own) - 1;
+          own &= own - 1u;
+          const int64_t pos = wb + 128 * c + 4 * lane + q;
+          s2d[pos] = dd;
+          perm[dd] = static_cast<int32_t>(pos);
+          ++dd;
+        }
+        d += __popc(b0) + __popc(b1) + __popc(b2) + __popc(b3);
+      }
+      base[j] += tot[j];
+    }
+  }
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int j = 0; j < kRbeExperts; ++j)
+      if (e0 + j <= E) offsets[e0 + j] = off[j];
+  }
+}
+
 // ---- row copy ------------------------------------------------------------------
 
 constexpr int kCopyThreads = 128;
@@ -530,6 +694,19 @@ lsek_status launch_route(const int32_t* idx, int64_t n, int E, int32_t* offsets,
   return check_launch("moe_permute(route)");
 }
 
+// Routing in one launch with no workspace (route_by_expert_kernel).
+lsek_status launch_route_by_expert(const int32_t* idx, int64_t n, int E, int32_t* offsets,
+                                   int32_t* s2d, int32_t* perm, cudaStream_t st) {
+  int64_t threads = ceil_div(n, kRbeWarpKeys) * 32;
+  if (threads < 32) threads = 32;
+  if (threads > 1024) threads = 1024;
+  const int grid = static_cast<int>(ceil_div(E + 1, kRbeExperts));
+  const int vec_ok = reinterpret_cast<uintptr_t>(idx) % 16 == 0;
+  route_by_expert_kernel<<<grid, static_cast<unsigned>(threads), 0, st>>>(idx, n, E, vec_ok,
+                                                                         offsets, s2d, perm);
+  return check_launch("moe_permute(route)");
+}
+
 lsek_status launch_permute_rows(void* dst, const void* src, const int32_t* s2d, int64_t T,
                                 int topk, int64_t row_bytes, cudaStream_t st) {
   if (row_bytes % 16 == 0 && reinterpret_cast<uintptr_t>(dst) % 16 == 0 &&
@@ -667,6 +844,28 @@ extern "C" lsek_status lsek_moe_permute(void* permuted_input, int32_t* expert_of
   if (hidden_dim == 0) return LSEK_OK;
   return launch_permute_rows(permuted_input, hidden_states, src_to_dest_map, num_tokens, topk,
                              static_cast<int64_t>(hidden_dim) * elem_size_bytes, st);
+}
+
+extern "C" lsek_status lsek_moe_route(int32_t* expert_offsets, int32_t* src_to_dest_map,
+                                      int32_t* permuted_idx, const int32_t* topk_indices,
+                                      int32_t num_tokens, int32_t topk, int32_t num_experts,
+                                      void* stream) {
+  LSEK_REQUIRE(num_tokens >= 0 && topk >= 0, "moe_route: sizes must be >= 0");
+  LSEK_REQUIRE(num_experts >= 1, "moe_route: num_experts must be >= 1");
+  if (num_experts > 1023)
+    return fail(LSEK_ERR_UNSUPPORTED, "moe_route: num_experts must be <= 1023");
+  LSEK_REQUIRE(topk <= 32, "moe_route: topk must be <= 32");
+  LSEK_REQUIRE(expert_offsets != nullptr, "moe_route: expert_offsets is NULL");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t n = static_cast<int64_t>(num_tokens) * topk;
+  LSEK_REQUIRE(n < (1ll << 31), "moe_route: num_tokens * topk must fit in int32");
+  if (n == 0) {
+    LSEK_CUDA_TRY(cudaMemsetAsync(expert_offsets, 0, sizeof(int32_t) * (num_experts + 1), st));
+    return LSEK_OK;
+  }
+  LSEK_REQUIRE(src_to_dest_map && permuted_idx && topk_indices, "moe_route: NULL tensor pointer");
+  return launch_route_by_expert(topk_indices, n, num_experts, expert_offsets, src_to_dest_map,
+                                permuted_idx, st);
 }
 
 extern "C" lsek_status lsek_moe_permute_noalloc(void* permuted_input, int32_t* expert_offsets,

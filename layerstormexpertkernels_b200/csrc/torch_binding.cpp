@@ -95,6 +95,25 @@ std::vector<torch::Tensor> moe_permute(torch::Tensor hidden_states, torch::Tenso
   return {permuted, offsets, s2d, perm};
 }
 
+// Routing only (lsek_moe_route): [expert_offsets int32[E+1], src_to_dest_map
+// int32[T*k], permuted_idx int32[T*k]], the maps moe_permute returns.
+std::vector<torch::Tensor> moe_route(torch::Tensor topk_indices, int64_t num_experts) {
+  TORCH_CHECK(topk_indices.is_cuda(), "moe_route: topk_indices must be on CUDA");
+  TORCH_CHECK(topk_indices.is_contiguous(), "moe_route: topk_indices must be contiguous");
+  TORCH_CHECK(topk_indices.dim() == 2, "moe_route: topk_indices must be 2D [num_tokens, topk]");
+  TORCH_CHECK(topk_indices.scalar_type() == at::kInt, "moe_route: topk_indices must be int32");
+  const c10::cuda::OptionalCUDAGuard guard(topk_indices.device());
+  const int64_t T = topk_indices.size(0), k = topk_indices.size(1);
+  auto offsets = torch::empty({num_experts + 1}, topk_indices.options());
+  auto s2d = torch::empty({T * k}, topk_indices.options());
+  auto perm = torch::empty({T * k}, topk_indices.options());
+  check_status(lsek_moe_route(offsets.data_ptr<int32_t>(), s2d.data_ptr<int32_t>(),
+                              perm.data_ptr<int32_t>(), topk_indices.data_ptr<int32_t>(),
+                              to_i32(T, "num_tokens"), to_i32(k, "topk"),
+                              to_i32(num_experts, "num_experts"), stream_of(topk_indices)));
+  return {offsets, s2d, perm};
+}
+
 void check_unpermute_args(const char* op, const torch::Tensor& permuted_output,
                           const torch::Tensor& topk_weights, const torch::Tensor& s2d,
                           int64_t num_tokens, int64_t topk) {
@@ -729,6 +748,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &moe_permute, py::arg("hidden_states"), py::arg("topk_indices"),
         py::arg("num_experts"),
         "MoE permute: sort tokens by expert. Returns (permuted, offsets, s2d_map, perm_idx).");
+  m.def("moe_route", &moe_route, py::arg("topk_indices"), py::arg("num_experts"),
+        "routing maps of moe_permute without the row copy: [expert_offsets, src_to_dest_map, "
+        "permuted_idx]");
   m.def("moe_unpermute", &moe_unpermute, py::arg("permuted_output"), py::arg("topk_weights"),
         py::arg("src_to_dest_map"), py::arg("num_tokens"), py::arg("topk"),
         "MoE unpermute: weighted reduction back to original order.");

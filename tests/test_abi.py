@@ -103,6 +103,31 @@ def test_permute_invalid_args(lib):
     assert st == LSEK_ERR_UNSUPPORTED
 
 
+def test_route_invalid_args(lib):
+    d = ctypes.c_void_p(16)
+    assert lib.lsek_moe_route(d, d, d, d, 4, 33, 256, None) == LSEK_ERR_INVALID_ARG
+    assert b"topk" in lib.lsek_last_error()
+    assert lib.lsek_moe_route(d, d, d, d, -1, 8, 256, None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_moe_route(d, d, d, d, 4, 8, 0, None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_moe_route(None, d, d, d, 4, 8, 256, None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_moe_route(d, None, d, d, 4, 8, 256, None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_moe_route(d, d, d, d, 4, 8, 1024, None) == LSEK_ERR_UNSUPPORTED
+
+
+def test_noalloc_permute_size_limit(lib):
+    """The static-buffer permute rejects, before touching the GPU, the first
+    size past its 1 MiB of route counts: at E=256 that is one slot past
+    2,088,960 (1021 chunks of 2048 slots x 257 counts x 4 bytes)."""
+    d = ctypes.c_void_p(256)
+    limit = 1 << 20  # LSEK_NOALLOC_PERMUTE_SCRATCH_BYTES
+    assert ((2_088_960 + 2047) // 2048) * 257 * 4 <= limit
+    assert ((2_088_961 + 2047) // 2048) * 257 * 4 > limit
+    st = lib.lsek_moe_permute_noalloc(d, d, d, d, d, d, 2_088_961, 1, 8, 256, 2, None)
+    assert st == LSEK_ERR_INVALID_ARG and b"static buffer" in lib.lsek_last_error()
+    st = lib.lsek_moe_permute_noalloc(d, d, d, d, d, d, 261121, 8, 8, 256, 2, None)
+    assert st == LSEK_ERR_INVALID_ARG and b"static buffer" in lib.lsek_last_error()
+
+
 def test_unpermute_topk_limit(lib):
     d = ctypes.c_void_p(16)
     st = lib.lsek_moe_unpermute(d, d, d, d, 4, 33, 64, 0, 0, None)

@@ -101,6 +101,65 @@ def test_permute_properties_full_size(T):
     assert torch.equal(back.view(torch.int16), hidden.view(torch.int16))
 
 
+# ---- routing only (moe_route) ----------------------------------------------------
+
+@pytest.mark.parametrize("name", ["t128_k4_e32", "t96_k8_e64_sentinels", "t1_k8_e256",
+                                  "t4096_k8_e256"])
+def test_route_golden(golden_dir, name):
+    d = np.load(os.path.join(golden_dir, f"permute_{name}.npz"))
+    import layerstormexpertkernels_b200 as P
+    off, s2d, perm = P.moe_route(dev(d["topk_indices"]), int(d["num_experts"]))
+    assert np.array_equal(perm.cpu().numpy(), d["perm"])
+    assert np.array_equal(s2d.cpu().numpy(), d["s2d"])
+    assert np.array_equal(off.cpu().numpy(), d["offsets"])
+
+
+@pytest.mark.parametrize("T,k,E,sent", [
+    (1, 1, 1, 0.0), (2, 8, 256, 0.0), (31, 3, 5, 0.2), (33, 8, 256, 0.0), (128, 8, 256, 0.0),
+    (4096, 8, 256, 0.0), (4097, 8, 256, 0.05), (8192, 8, 256, 0.0), (20000, 6, 1023, 0.01),
+    (3, 32, 64, 0.0), (1, 8, 1023, 0.5), (65536, 8, 256, 0.001), (4095, 8, 2, 0.0),
+])
+def test_route_vs_oracle(T, k, E, sent):
+    """One launch, one CTA per two experts, every CTA reading all T*k keys:
+    maps and offsets bit-exact against the oracle's stable sort, including
+    sentinel keys, E = 1023 (512 CTAs), an odd expert count (the last CTA's
+    second slot is past the sentinel bin), a key count that is not a multiple
+    of 32, and 524288 keys (16 rounds of 32768 per CTA)."""
+    import layerstormexpertkernels_b200 as P
+    idx = cases.permute_indices(T, k, E, sent, seed=T * 7 + k)
+    off, s2d, perm = P.moe_route(idx.cuda(), E)
+    _, ooff, os2d, operm = O.moe_permute(None, idx.numpy(), E)
+    assert np.array_equal(perm.cpu().numpy(), operm)
+    assert np.array_equal(s2d.cpu().numpy(), os2d)
+    assert np.array_equal(off.cpu().numpy(), ooff)
+
+
+def test_route_unaligned_indices_and_matches_permute():
+    """topk_indices that start 4 bytes past a 16-byte boundary take the
+    scalar key loads; the maps equal moe_permute's."""
+    import layerstormexpertkernels_b200 as P
+    idx = cases.permute_indices(3000, 8, 256, 0.01, seed=9)
+    buf = torch.empty(3000 * 8 + 1, dtype=torch.int32, device="cuda")
+    buf[1:] = idx.cuda().view(-1)
+    view = buf[1:].view(3000, 8)
+    assert view.data_ptr() % 16 != 0
+    off, s2d, perm = P.moe_route(view, 256)
+    hidden = rand_bf16((3000, 32), seed=2).cuda()
+    _, poff, ps2d, pperm = ek().moe_permute(hidden, idx.cuda(), 256)
+    assert torch.equal(off, poff) and torch.equal(s2d, ps2d) and torch.equal(perm, pperm)
+
+
+def test_route_zero_tokens_and_rejections():
+    import layerstormexpertkernels_b200 as P
+    off, s2d, perm = P.moe_route(torch.empty(0, 8, dtype=torch.int32).cuda(), 16)
+    torch.cuda.synchronize()
+    assert off.shape == (17,) and int(off.abs().sum()) == 0 and s2d.numel() == 0
+    with pytest.raises(RuntimeError):
+        P.moe_route(torch.zeros(4, 8, dtype=torch.int32).cuda(), 1024)
+    with pytest.raises(ValueError):
+        P.moe_route(torch.zeros(4, 33, dtype=torch.int32).cuda(), 16)
+
+
 def test_reference_roundtrip_case():
     # tests/test_kernels.py:58-88
     B, D, E, k = 128, 512, 32, 4

@@ -75,6 +75,21 @@ def test_noalloc_permute_matches_workspace_permute_on_two_calls():
             assert torch.equal(a, b), f"{name} differs at T={T}, E={E}"
 
 
+def test_noalloc_permute_at_its_largest_size():
+    """The largest request the static buffer holds at E=256: 261120 tokens at
+    top-8 (2,088,960 slots = 1020 route chunks of 2048, times 257 counts of
+    4 bytes = exactly 1 MiB).  Bits equal the workspace permute's."""
+    lib = load_lib()
+    T, k, E, H = 261120, 8, 256, 8
+    g = torch.Generator().manual_seed(3)
+    idx = torch.randint(0, E, (T, k), generator=g, dtype=torch.int32).cuda()
+    hidden = torch.randn(T, H, generator=g).to(torch.bfloat16).cuda()
+    got = run_permute(lib, hidden, idx, E, noalloc=True)
+    want = run_permute(lib, hidden, idx, E, noalloc=False)
+    for name, a, b in zip(("permuted", "offsets", "src_to_dest", "permuted_idx"), got, want):
+        assert torch.equal(a, b), f"{name} differs at the largest size"
+
+
 def test_noalloc_permute_rejects_sizes_beyond_its_buffer():
     lib = load_lib()
     d = ctypes.c_void_p(256)  # never dereferenced: the size check fails first
