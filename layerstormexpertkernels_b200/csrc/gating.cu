@@ -1,15 +1,18 @@
 // Top-k gating and adaptive gating for sm_100a.
 //
-// Top-k gating keeps one token per warp.  Lane l owns the EPL consecutive
-// experts [l*EPL, (l+1)*EPL), loaded with 16-byte vector loads, so one warp
-// reads a token's logits row as one contiguous 1 KB (E=256) burst and every
-// later phase runs in registers:
+// Top-k gating gives each token a segment of LPT lanes: 16 (two tokens per
+// warp, so each selection-round instruction below serves both) when E <= 128,
+// topk <= 16 and n_group <= 16, else the whole warp, as at DeepSeek-V3 shape.
+// Lane l of a segment owns the EPL consecutive experts [l*EPL, (l+1)*EPL),
+// loaded (with the bias) as 16-byte vectors, so a segment reads a token's
+// logits row as one contiguous 1 KB (E=256) burst and every later phase runs
+// in registers:
 //   1. score   s = sigmoid(x) or sqrt(softplus(x)); sel = s + bias
 //   2. groups  (n_group > 1) per-group sum of the top-2 sel values, then each
 //              lane g computes its group's rank among all groups with
 //              shuffles (ties go to the lower group) and a ballot gives the
 //              kept-group mask; experts of dropped groups leave the race
-//   3. top-k   topk rounds of a warp arg-max on (order-preserving key of sel,
+//   3. top-k   topk rounds of a segment arg-max on (order-preserving key of sel,
 //              expert id), ties to the lower id; the owning lane retires its
 //              winner and rescans its EPL candidates
 //   4. weights unbiased score of each winner, summed in selection order,
@@ -36,7 +39,7 @@ constexpr unsigned kFull = 0xffffffffu;
 
 __device__ __forceinline__ float score_sigmoid(float x) {
   const float e = static_cast<float>(exp(-static_cast<double>(x)));
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+  return __frcp_rn(__fadd_rn(1.0f, e));  // the correctly rounded 1 / (1 + e)
 }
 
 // sqrt(softplus(x)) with torch's softplus threshold: x > 20 -> x, else
@@ -68,34 +71,54 @@ __device__ __forceinline__ void merge_top2(float& t1, float& t2, float o1, float
   }
 }
 
-template <int EPL>
-__global__ void __launch_bounds__(256, 3) topk_gating_kernel(
+// LPT lanes per token (32, or 16 so that one warp serves two tokens and
+// every instruction of the selection rounds below works for both); lane l of
+// a token's segment owns the EPL consecutive experts [l*EPL, (l+1)*EPL).
+// Segment-wide reductions use the segment's lane mask, shuffles a width of
+// LPT.  The token loop is uniform across the warp, so a segment whose token
+// is past the end still takes part in every shuffle (on row 0's values) and
+// only skips the stores.
+template <int EPL, int LPT>
+__global__ void __launch_bounds__(256, (LPT == 16 || EPL >= 16) ? (EPL >= 16 && LPT == 32 ? 1 : 2) : 3) topk_gating_kernel(
     float* __restrict__ out_w, int32_t* __restrict__ out_i,
     const float* __restrict__ logits, const float* __restrict__ bias, int T,
     int E, int topk, int n_group, int topk_group, float rsf, int renorm,
     int scoring, int vec_ok, int seg_lanes) {
-  extern __shared__ float s_group[];  // per warp: sel values, padded 33/32 (general path)
+  constexpr int TPW = 32 / LPT;  // tokens per warp
+  extern __shared__ float s_group[];  // per token slot: sel values, padded 33/32 (general path)
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int warps_per_block = blockDim.x >> 5;
+  const int sub = lane / LPT;  // token slot in the warp
+  const int l = lane % LPT;    // lane in the token's segment
+  const unsigned seg_mask = LPT == 32 ? kFull : (((1u << (LPT & 31)) - 1u) << (sub * LPT));
   const int pad_stride = E + (E >> 5) + 1;
-  float* s_sel = s_group + warp * pad_stride;
-  const int e0 = lane * EPL;
+  float* s_sel = s_group + (warp * TPW + sub) * pad_stride;
+  const int e0 = l * EPL;
   const int epg = E / n_group;
 
-  for (int t = blockIdx.x * warps_per_block + warp; t < T;
-       t += gridDim.x * warps_per_block) {
-    const float* row = logits + static_cast<int64_t>(t) * E;
-    float x[EPL];
+  for (int wt = blockIdx.x * warps_per_block + warp; wt * TPW < T;
+       wt += gridDim.x * warps_per_block) {
+    const int t = wt * TPW + sub;
+    const bool tok = t < T;
+    const float* row = logits + static_cast<int64_t>(tok ? t : 0) * E;
+    float x[EPL], bv[EPL];
     if (EPL >= 4 && vec_ok && e0 + EPL <= E) {
 #pragma unroll
       for (int j = 0; j < EPL; j += 4) {
         const float4 v = __ldg(reinterpret_cast<const float4*>(row + e0 + j));
         x[j] = v.x; x[j + 1] = v.y; x[j + 2] = v.z; x[j + 3] = v.w;
+        const float4 b = bias != nullptr ? __ldg(reinterpret_cast<const float4*>(bias + e0 + j))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        bv[j] = b.x; bv[j + 1] = b.y; bv[j + 2] = b.z; bv[j + 3] = b.w;
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < EPL; ++j) x[j] = (e0 + j < E) ? __ldg(row + e0 + j) : 0.0f;
+      for (int j = 0; j < EPL; ++j) {
+        const bool in = e0 + j < E;
+        x[j] = in ? __ldg(row + e0 + j) : 0.0f;
+        bv[j] = (in && bias != nullptr) ? __ldg(bias + e0 + j) : 0.0f;
+      }
     }
 
     // x[] becomes the biased selection score; sc[] keeps the unbiased score.
@@ -103,10 +126,10 @@ __global__ void __launch_bounds__(256, 3) topk_gating_kernel(
 #pragma unroll
     for (int j = 0; j < EPL; ++j) {
       const int e = e0 + j;
-      const float s = scoring == LSEK_SCORING_SIGMOID ? score_sigmoid(x[j])
-                                                      : score_sqrtsoftplus(x[j]);
-      sc[j] = s;
-      x[j] = (e >= E) ? -INFINITY : (bias != nullptr ? __fadd_rn(s, __ldg(bias + e)) : s);
+      const float sv = scoring == LSEK_SCORING_SIGMOID ? score_sigmoid(x[j])
+                                                       : score_sqrtsoftplus(x[j]);
+      sc[j] = sv;
+      x[j] = (e >= E) ? -INFINITY : (bias != nullptr ? __fadd_rn(sv, bv[j]) : sv);
     }
     uint32_t key[EPL];
 #pragma unroll
@@ -116,7 +139,7 @@ __global__ void __launch_bounds__(256, 3) topk_gating_kernel(
       bool kept_mine[EPL];
       if (seg_lanes > 0) {
         // Each lane's experts lie in one group and a group spans seg_lanes
-        // aligned lanes: top-2 by xor-shuffles inside the segment.
+        // aligned lanes: top-2 by xor-shuffles inside the group.
         float t1 = -INFINITY, t2 = -INFINITY;
 #pragma unroll
         for (int j = 0; j < EPL; ++j) merge_top2(t1, t2, x[j], -INFINITY);
@@ -126,10 +149,10 @@ __global__ void __launch_bounds__(256, 3) topk_gating_kernel(
           merge_top2(t1, t2, o1, o2);
         }
         const float mine = (epg >= 2) ? __fadd_rn(t1, t2) : t1;
-        const int g_me = lane / seg_lanes;
+        const int g_me = l / seg_lanes;
         int rank = 0;
         for (int h = 0; h < n_group; ++h) {
-          const float o = __shfl_sync(kFull, mine, h * seg_lanes);
+          const float o = __shfl_sync(kFull, mine, h * seg_lanes, LPT);
           rank += (o > mine) || (o == mine && h < g_me);
         }
 #pragma unroll
@@ -143,9 +166,9 @@ __global__ void __launch_bounds__(256, 3) topk_gating_kernel(
         }
         __syncwarp();
         float gscore = 0.0f;
-        if (lane < n_group) {
+        if (l < n_group) {
           float t1 = -INFINITY, t2 = -INFINITY;
-          const int gb = lane * epg;
+          const int gb = l * epg;
           for (int i = 0; i < epg; ++i) {
             const int e = gb + i;
             merge_top2(t1, t2, s_sel[e + (e >> 5)], -INFINITY);
@@ -154,10 +177,11 @@ __global__ void __launch_bounds__(256, 3) topk_gating_kernel(
         }
         int rank = 0;
         for (int h = 0; h < n_group; ++h) {
-          const float o = __shfl_sync(kFull, gscore, h);
-          rank += (o > gscore) || (o == gscore && h < lane);
+          const float o = __shfl_sync(kFull, gscore, h, LPT);
+          rank += (o > gscore) || (o == gscore && h < l);
         }
-        const unsigned kept = __ballot_sync(kFull, lane < n_group && rank < topk_group);
+        const unsigned kept_all = __ballot_sync(kFull, l < n_group && rank < topk_group);
+        const unsigned kept = LPT == 32 ? kept_all : (kept_all >> (sub * LPT));
 #pragma unroll
         for (int j = 0; j < EPL; ++j) {
           const int e = e0 + j;
@@ -181,18 +205,19 @@ __global__ void __launch_bounds__(256, 3) topk_gating_kernel(
     float my_w = 0.0f;
     int my_i = 0;
     for (int k = 0; k < topk; ++k) {
-      // Warp arg-max: the highest key (one redux), and among the lanes that
-      // hold it the lowest one, whose experts have the lowest ids (each lane
-      // already keeps its lowest j on ties).
-      const uint32_t kmax = __reduce_max_sync(kFull, bk);
-      const int owner = __ffs(__ballot_sync(kFull, bk == kmax)) - 1;
-      const int ie = owner * EPL + __shfl_sync(kFull, bj, owner);
+      // Segment arg-max: the highest key (one redux), and among the lanes
+      // that hold it the lowest one, whose experts have the lowest ids (each
+      // lane already keeps its lowest j on ties).
+      const uint32_t kmax = __reduce_max_sync(seg_mask, bk);
+      const unsigned hit = __ballot_sync(kFull, bk == kmax);
+      const int owner = __ffs(LPT == 32 ? hit : (hit >> (sub * LPT)) & ((1u << (LPT & 31)) - 1u)) - 1;
+      const int ie = owner * EPL + __shfl_sync(kFull, bj, owner, LPT);
       float mine = 0.0f;
 #pragma unroll
       for (int j = 0; j < EPL; ++j)
         if (j == bj) mine = sc[j];
-      const float wv = __shfl_sync(kFull, mine, owner);
-      if (lane == owner) {
+      const float wv = __shfl_sync(kFull, mine, owner, LPT);
+      if (l == owner) {
 #pragma unroll
         for (int j = 0; j < EPL; ++j)
           if (j == bj) key[j] = 0u;
@@ -203,20 +228,21 @@ __global__ void __launch_bounds__(256, 3) topk_gating_kernel(
           if (key[j] > bk) { bk = key[j]; bj = j; }
       }
       wsum = __fadd_rn(wsum, wv);
-      if (lane == k) { my_w = wv; my_i = ie; }
+      if (l == k) { my_w = wv; my_i = ie; }
     }
     if (renorm && wsum > 0.0f) my_w = __fmul_rn(my_w, __fdiv_rn(rsf, wsum));
-    if (lane < topk) {
-      out_w[static_cast<int64_t>(t) * topk + lane] = my_w;
-      out_i[static_cast<int64_t>(t) * topk + lane] = my_i;
+    if (tok && l < topk) {
+      out_w[static_cast<int64_t>(t) * topk + l] = my_w;
+      out_i[static_cast<int64_t>(t) * topk + l] = my_i;
     }
   }
 }
 
-template <int EPL>
+template <int EPL, int LPT>
 cudaError_t launch_topk(float* w, int32_t* idx, const float* logits,
                         const float* bias, const lsek_topk_gating_params& p,
                         int vec_ok, cudaStream_t st) {
+  constexpr int TPW = 32 / LPT;
   const int threads = 256;
   const int warps = threads / 32;
   // Register path for groups: every lane's EPL experts in one group and a
@@ -225,32 +251,32 @@ cudaError_t launch_topk(float* w, int32_t* idx, const float* logits,
   if (p.n_group > 1) {
     const int epg = p.num_experts / p.n_group;
     const int lanes = epg / EPL;
-    if (p.num_experts == 32 * EPL && epg % EPL == 0 && lanes >= 1 && (lanes & (lanes - 1)) == 0)
+    if (p.num_experts == LPT * EPL && epg % EPL == 0 && lanes >= 1 && (lanes & (lanes - 1)) == 0)
       seg = lanes;
   }
-  const size_t smem =
-      (p.n_group > 1 && seg == 0)
-          ? static_cast<size_t>(warps) * (p.num_experts + (p.num_experts >> 5) + 1) * sizeof(float)
-          : 0;
-  // One wave of resident blocks at most (one warp per token, so a token's
-  // latency chain is the kernel's critical path: no warp takes two tokens
-  // while the SMs could hold more).
-  // (The register-path occupancy is cached: the query is a driver call.)
+  const size_t smem = (p.n_group > 1 && seg == 0)
+                          ? static_cast<size_t>(warps) * TPW *
+                                (p.num_experts + (p.num_experts >> 5) + 1) * sizeof(float)
+                          : 0;
+  // One wave of resident blocks at most: a token's latency chain is the
+  // kernel's critical path, so no warp takes a second pair of tokens while
+  // the SMs could hold more warps.  (The register-path occupancy is cached:
+  // the query is a driver call.)
   static std::atomic<int> cached_per_sm{0};
   int per_sm = smem == 0 ? cached_per_sm.load(std::memory_order_relaxed) : 0;
   if (per_sm == 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, topk_gating_kernel<EPL>, threads,
-                                                      smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, topk_gating_kernel<EPL, LPT>,
+                                                      threads, smem) != cudaSuccess ||
         per_sm < 1) {
       cudaGetLastError();  // a failed query must not read as a failed launch
       per_sm = 1;
     }
     if (smem == 0) cached_per_sm.store(per_sm, std::memory_order_relaxed);
   }
-  const int blocks_needed = static_cast<int>(ceil_div(p.num_tokens, warps));
+  const int blocks_needed = static_cast<int>(ceil_div(ceil_div(p.num_tokens, TPW), warps));
   const int cap = num_sms() * per_sm;
   const int grid = blocks_needed < cap ? blocks_needed : cap;
-  topk_gating_kernel<EPL><<<grid, threads, smem, st>>>(
+  topk_gating_kernel<EPL, LPT><<<grid, threads, smem, st>>>(
       w, idx, logits, bias, p.num_tokens, p.num_experts, p.topk,
       p.n_group > 1 ? p.n_group : 1, p.topk_group, p.routed_scaling_factor,
       p.renormalize, p.scoring_func, vec_ok, seg);
@@ -340,15 +366,30 @@ extern "C" lsek_status lsek_topk_gating(float* topk_weights,
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int vec_ok = (p.num_experts % 4 == 0) &&
-                     (reinterpret_cast<uintptr_t>(logits) % 16 == 0);
-  const int epl = static_cast<int>(ceil_div(p.num_experts, 32));
+                     (reinterpret_cast<uintptr_t>(logits) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(bias) % 16 == 0);
+  // Two tokens per warp (16 lanes each) when a token's experts, selections
+  // and groups fit in 16 lanes at no more than 8 experts a lane; else one
+  // token per warp.  (At E=256, 16 experts a lane doubled the registers and
+  // the unrolled code and measured 22 us against 14 us for one token per
+  // warp, the same instruction count at half the resident warps.)
+  const bool half = p.num_experts <= 128 && p.topk <= 16 && p.n_group <= 16;
   cudaError_t e;
-  if (epl <= 1)       e = launch_topk<1>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
-  else if (epl <= 2)  e = launch_topk<2>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
-  else if (epl <= 4)  e = launch_topk<4>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
-  else if (epl <= 8)  e = launch_topk<8>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
-  else if (epl <= 16) e = launch_topk<16>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
-  else                e = launch_topk<32>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+  if (half) {
+    const int epl = static_cast<int>(ceil_div(p.num_experts, 16));
+    if (epl <= 1)      e = launch_topk<1, 16>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+    else if (epl <= 2) e = launch_topk<2, 16>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+    else if (epl <= 4) e = launch_topk<4, 16>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+    else               e = launch_topk<8, 16>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+  } else {
+    const int epl = static_cast<int>(ceil_div(p.num_experts, 32));
+    if (epl <= 1)       e = launch_topk<1, 32>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+    else if (epl <= 2)  e = launch_topk<2, 32>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+    else if (epl <= 4)  e = launch_topk<4, 32>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+    else if (epl <= 8)  e = launch_topk<8, 32>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+    else if (epl <= 16) e = launch_topk<16, 32>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+    else                e = launch_topk<32, 32>(topk_weights, topk_indices, logits, bias, p, vec_ok, st);
+  }
   if (e != cudaSuccess) return fail(LSEK_ERR_CUDA, "topk_gating: %s", cudaGetErrorString(e));
   return LSEK_OK;
 }

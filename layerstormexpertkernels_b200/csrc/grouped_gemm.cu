@@ -107,37 +107,40 @@ constexpr int kUnitQ = 4;                      // unit ids in flight between war
 constexpr int kSwapMaxRows = 64;               // tiles this small use swapped operands
 constexpr int kA16Bytes = 16 * kBK * 2;        // one 16-row A box (2 KB)
 
-// Pipeline geometry.  Each k-block of a unit is one stage: its A box (token
-// rows; two A boxes for a paired unit) followed by two 128-row weight boxes.
-// Stages are laid out back to back in a byte ring of RING_BYTES, so a paired
-// unit's larger stages and a single unit's smaller ones share the ring
-// without padding; each stage has one full and one empty barrier (a ring of
-// kRecs records).  A box starting near the end of the ring continues at its
-// start, so the ring length must keep every box whole: a multiple of the box
-// size (full geometry), or of the one stage size when every stage is alike.
-// A_ROWS is the token rows of the A box, MAX_E the largest expert count the
-// unit table holds.
+// Pipeline geometry.  Each k-block of a unit is one stage: two 128-row
+// weight boxes (adjacent, one N=256 MMA reads both) and the A rows of its
+// tile (of both tiles for a paired unit).  A full tile's A rows are one
+// 16 KB box; a swapped tile needs only its rows rounded up to 16, so its A
+// part is that many 2 KB (16-row) boxes and its stage takes only the bytes
+// it loads: 48 KB for a single full tile, 34-40 KB for a small expert's
+// tile, 50-56 KB for the usual DeepSeek-V3 pair of a full tile and a few
+// rows, 64 KB for two full tiles.  Stages lie back to back in a byte ring of
+// RING_BYTES; a box that would cross the ring's end starts at its beginning
+// instead (the skipped tail counts towards that stage), and every part of a
+// stage starts on a 1024-byte boundary as the 128-byte swizzle needs.  Each
+// stage has one full and one empty barrier (a ring of kRecs records).
+// A_ROWS is the token rows of the tiled A box, MAX_E the largest expert
+// count the unit table holds.
 template <int RING_BYTES, int A_ROWS, int MAX_E>
 struct Geom {
   static constexpr int kRingBytes = RING_BYTES;
   static constexpr int kARows = A_ROWS;
   static constexpr int kABytes = A_ROWS * kBK * 2;
-  static constexpr int kStageBytes = kABytes + 2 * kBoxBytes;  // a single unit's stage
-  static constexpr int kPairStageBytes = 2 * kABytes + 2 * kBoxBytes;
   static constexpr int kMaxE = MAX_E;
   static constexpr int kRecs = 8;  // more than the stages that fit in the ring
   // Every tile has at most kARows rows, so every tile is a swapped small tile.
   static constexpr bool kSmallOnly = A_ROWS <= kSwapMaxRows;
   // Units may cover two m-tiles of an expert (M = 256 against one weight tile).
   static constexpr bool kPairs = !kSmallOnly;
-  static_assert(kABytes % 1024 == 0, "swizzled boxes start on 1024-byte boundaries");
-  static_assert(kPairs ? (kABytes == kBoxBytes && RING_BYTES % kBoxBytes == 0)
-                       : RING_BYTES % kStageBytes == 0,
-                "every box must lie whole inside the ring");
-  static_assert(kRecs * kStageBytes > RING_BYTES, "a record is reused only after its stage left");
+  // The smallest stage: the weight boxes and one 16-row A box (or the tiled
+  // A box of the decode geometry).
+  static constexpr int kMinStageBytes = 2 * kBoxBytes + (kSmallOnly ? kABytes : 16 * kBK * 2);
+  static_assert(kABytes % 1024 == 0 && RING_BYTES % 1024 == 0,
+                "swizzled boxes start on 1024-byte boundaries");
+  static_assert(RING_BYTES >= 2 * kBoxBytes + 2 * kABytes, "the largest stage fits the ring");
+  static_assert(kRecs * kMinStageBytes > RING_BYTES, "a record is reused only after its stage left");
 };
-// Any routing: a 208 KB ring, four 48 KB single stages or three 64 KB paired
-// stages in flight.
+// Any routing: a 208 KB ring, four to six stages in flight.
 using GeomFull = Geom<13 * kBoxBytes, 128, kMaxExperts>;
 // Decode (every expert has at most 32 rows): a 4 KB token box, six 36 KB
 // stages in flight.
@@ -195,6 +198,7 @@ struct SmemT {
   uint64_t q_full[kUnitQ];
   uint64_t q_empty[kUnitQ];
   int32_t unit_q[kUnitQ];
+  uint32_t span[G::kRecs];  // ring bytes of each outstanding stage (producer only)
   uint32_t tmem_base;
   int32_t abort;
   int32_t warp_tot[kThreads / 32];
@@ -399,6 +403,16 @@ __device__ __forceinline__ Unit decode_unit(const S& s, int num_experts, int id,
   return u;
 }
 
+// A bytes of one tile in a stage: a full tile's 128-row box, the tiled box
+// of the decode geometry, or a swapped tile's rows rounded up to 16.
+template <class G>
+__device__ __forceinline__ uint32_t tile_a_bytes(int rows, bool gathered) {
+  const bool swapped = G::kSmallOnly || rows <= kSwapMaxRows;
+  if (!swapped) return static_cast<uint32_t>(kBM * kBK * 2);
+  if (G::kSmallOnly && !gathered) return static_cast<uint32_t>(G::kABytes);
+  return static_cast<uint32_t>(((rows + 15) & ~15) * kBK * 2);
+}
+
 // Position in the stage ring: stage j uses record j % kRecs (barrier parity
 // (j / kRecs) & 1) and starts at byte `off` of the ring.  Producer and MMA
 // issuer walk the same stage sequence and each keeps its own copy.
@@ -408,30 +422,41 @@ struct RingPos {
   uint32_t off = 0;  // ring offset of stage j
   __device__ __forceinline__ int rec() const { return static_cast<int>(j % G::kRecs); }
   __device__ __forceinline__ uint32_t parity() const { return (j / G::kRecs) & 1u; }
-  // Ring address of byte `at` of the current stage.
-  __device__ __forceinline__ uint32_t at(uint32_t at_off) const {
-    const uint32_t o = off + at_off;
-    return o >= static_cast<uint32_t>(G::kRingBytes) ? o - G::kRingBytes : o;
-  }
-  __device__ __forceinline__ void advance(uint32_t bytes) {
+  __device__ __forceinline__ void advance(uint32_t span) {
     ++j;
-    off = at(bytes);
+    off += span;
+    if (off >= static_cast<uint32_t>(G::kRingBytes)) off -= G::kRingBytes;
   }
-  // Ring offsets of the current stage's boxes.  The two weight boxes go
-  // first and stay adjacent, so one N=256 MMA reads both; when the stage
-  // starts in the ring's last box the first A box takes that box and the
-  // weight boxes start the next lap.  A1 is the second A box of a paired
-  // unit.
-  __device__ __forceinline__ void layout(uint32_t& a0, uint32_t& a1, uint32_t& b0) const {
-    if (off + kBoxBytes == static_cast<uint32_t>(G::kRingBytes)) {
-      a0 = off;
-      b0 = 0;
-      a1 = 2u * kBoxBytes;
+  // Ring offsets of the current stage's parts: the weight boxes (b0, 32 KB),
+  // the first tile's A rows (a0, a0_bytes) and, for a paired unit, the
+  // second tile's (a1, a1_bytes; a1_bytes == 0 otherwise).  A part that
+  // would cross the ring end starts at 0; when the weight boxes do not fit
+  // before the end but the first A part does, that part goes first so the
+  // tail is used.  Returns the stage's span: its bytes plus any skipped tail.
+  __device__ __forceinline__ uint32_t layout(uint32_t a0_bytes, uint32_t a1_bytes, uint32_t& b0,
+                                             uint32_t& a0, uint32_t& a1) const {
+    constexpr uint32_t R = static_cast<uint32_t>(G::kRingBytes);
+    uint32_t cur = off, span = 0;
+    auto place = [&](uint32_t size) -> uint32_t {
+      if (cur + size > R) {
+        span += R - cur;
+        cur = 0;
+      }
+      const uint32_t at = cur;
+      cur += size;
+      span += size;
+      if (cur == R) cur = 0;
+      return at;
+    };
+    if (off + 2u * kBoxBytes > R && off + a0_bytes <= R) {
+      a0 = place(a0_bytes);
+      b0 = place(2u * kBoxBytes);
     } else {
-      b0 = off;
-      a0 = at(2u * kBoxBytes);
-      a1 = at(2u * kBoxBytes + G::kABytes);
+      b0 = place(2u * kBoxBytes);
+      a0 = place(a0_bytes);
     }
+    a1 = a1_bytes != 0u ? place(a1_bytes) : 0u;
+    return span;
   }
 };
 
@@ -531,27 +556,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       RingPos<G> pos;
       uint32_t j_free = 0;        // stages before this one have been released
       uint32_t held = 0;          // ring bytes of stages j_free .. pos.j - 1
-      uint32_t paired = 0;        // bit r: record r's outstanding stage is a paired unit's
       bool ok = true;
       int qslot = 0;
       uint32_t qphase = 0;
-      // Reserves `bytes` of ring for the next stage: releases the oldest
-      // stages (waiting for the MMA to free them) until the stage and its
-      // record are free, then arms its full barrier for `tx` bytes.  False
-      // on abort.
-      auto reserve = [&](uint32_t bytes, uint32_t tx) -> bool {
+      // Reserves `span` bytes of ring for the next stage: releases the
+      // oldest stages (waiting for the MMA to free them) until the stage and
+      // its record are free, then arms its full barrier for `tx` bytes.
+      // False on abort.
+      auto reserve = [&](uint32_t span, uint32_t tx) -> bool {
         while (pos.j - j_free >= static_cast<uint32_t>(kRecs) ||
-               held + bytes > static_cast<uint32_t>(G::kRingBytes)) {
+               held + span > static_cast<uint32_t>(G::kRingBytes)) {
           const int r = static_cast<int>(j_free % kRecs);
           if (!mbar_wait(&s.empty_bar[r], (j_free / kRecs) & 1u, abort, kDevErrGemmProducerWait,
                          true))
             return false;
-          held -= ((paired >> r) & 1u) ? G::kPairStageBytes : G::kStageBytes;
+          held -= s.span[r];
           ++j_free;
         }
-        const uint32_t bit = 1u << pos.rec();
-        paired = bytes == static_cast<uint32_t>(G::kPairStageBytes) ? (paired | bit) : (paired & ~bit);
-        held += bytes;
+        s.span[pos.rec()] = span;
+        held += span;
         mbar_expect_tx(&s.full_bar[pos.rec()], tx);
         return true;
       };
@@ -573,14 +596,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row0 = s.offs[u.e] + u.t0 * kBM;
         const int brow = u.e * p.b_rows + u.n * p.b_tile_rows;
         // A tile that runs with swapped operands needs only its rows rounded
-        // up to 16: it is loaded as that many 16-row boxes instead of one
-        // 128-row box (the stage keeps the full box's ring space).  Tiled A
-        // only; the first tile of a paired unit is always a full one.
+        // up to 16: tiled A loads them as that many 16-row boxes instead of
+        // one 128-row box.  The first tile of a paired unit is always full.
+        const bool gathered = p.gather_idx != nullptr;
         const int rows_t0 = tile_rows(s, u.e, u.t0);
         const int rows_t1 = u.pair ? tile_rows(s, u.e, u.t0 + 1) : 0;
-        const int n16_t0 = (!G::kSmallOnly && !u.pair && rows_t0 <= kSwapMaxRows && p.gather_idx == nullptr)
-                               ? (rows_t0 + 15) >> 4 : 0;
-        const int n16_t1 = (u.pair && rows_t1 <= kSwapMaxRows) ? (rows_t1 + 15) >> 4 : 0;
+        const uint32_t a0_bytes = tile_a_bytes<G>(rows_t0, gathered);
+        const uint32_t a1_bytes = u.pair ? tile_a_bytes<G>(rows_t1, gathered) : 0u;
+        const int n16_t0 = (!G::kSmallOnly && !gathered && rows_t0 <= kSwapMaxRows)
+                               ? static_cast<int>(a0_bytes / kA16Bytes) : 0;
+        const int n16_t1 = (u.pair && rows_t1 <= kSwapMaxRows)
+                               ? static_cast<int>(a1_bytes / kA16Bytes) : 0;
         // Gathered A: the MMA reads 128 rows (or, for a swapped small tile,
         // its rows rounded up to 16); rows past the expert repeat its first
         // row (their results are discarded).
@@ -591,22 +617,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int r = 0; r < nload; ++r)
             s.arow[r] = __ldg(p.gather_idx + row0 + (r < valid ? r : 0)) / p.gather_k;
         }
-        const uint32_t a_bytes = p.gather_idx != nullptr ? static_cast<uint32_t>(nload * kBK * 2)
-                                 : n16_t0 > 0           ? static_cast<uint32_t>(n16_t0 * kA16Bytes)
-                                                        : G::kABytes;
-        const uint32_t a1_bytes = !u.pair ? 0u
-                                  : n16_t1 > 0 ? static_cast<uint32_t>(n16_t1 * kA16Bytes)
-                                               : G::kABytes;
-        const uint32_t stage_bytes = u.pair ? G::kPairStageBytes : G::kStageBytes;
-        const uint32_t tx = a_bytes + a1_bytes + 2u * kBoxBytes;
+        const uint32_t tx = a0_bytes + a1_bytes + 2u * kBoxBytes;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!reserve(stage_bytes, tx)) {
+          uint32_t oa0, oa1, ob0;
+          const uint32_t span = pos.layout(a0_bytes, a1_bytes, ob0, oa0, oa1);
+          if (!reserve(span, tx)) {
             ok = false;
             break;
           }
           uint64_t* full = &s.full_bar[pos.rec()];
-          uint32_t oa0, oa1, ob0;
-          pos.layout(oa0, oa1, ob0);
           uint8_t* a0 = s.ring + oa0;
           if (p.gather_idx != nullptr) {
             for (int r = 0; r < nload; r += 4)
@@ -629,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tma_load_2d(s.ring + ob0, &tmap_b, full, kb * kBK, brow, pol_w);
           tma_load_2d(s.ring + ob0 + kBoxBytes, &tmap_b, full, kb * kBK, brow + p.b_second, pol_w);
-          pos.advance(stage_bytes);
+          pos.advance(span);
         }
       }
       if (!ok) {  // let every issued load land before the CTA can exit
@@ -679,7 +698,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d0 = tmem_base + static_cast<uint32_t>(acc0 * kBN);
         const uint32_t d1 = tmem_base + static_cast<uint32_t>(acc1 * kBN);
-        const uint32_t stage_bytes = u.pair ? G::kPairStageBytes : G::kStageBytes;
+        const bool gathered = p.gather_idx != nullptr;
+        const uint32_t a0_bytes = tile_a_bytes<G>(rows_here, gathered);
+        const uint32_t a1_bytes = u.pair ? tile_a_bytes<G>(rows1, gathered) : 0u;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           const int rec = pos.rec();
           if (!mbar_wait(&s.full_bar[rec], pos.parity(), abort, kDevErrGemmMmaWait, true)) {
@@ -688,7 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           uint32_t oa0, oa1, ob0;
-          pos.layout(oa0, oa1, ob0);
+          const uint32_t span = pos.layout(a0_bytes, a1_bytes, ob0, oa0, oa1);
           const uint32_t a0_addr = ring + oa0;
           const uint32_t a1_addr = ring + oa1;
           const uint32_t b0_addr = ring + ob0;
@@ -726,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           umma_commit(&s.empty_bar[rec]);
-          pos.advance(stage_bytes);
+          pos.advance(span);
         }
         if (ok) {
           umma_commit(&s.acc_full_bar[acc0]);

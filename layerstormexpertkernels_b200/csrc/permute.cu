@@ -294,25 +294,43 @@ constexpr int kRbeVecs = 8;                   // 16-byte key vectors per lane pe
 constexpr int kRbeKeys = 4 * kRbeVecs;        // keys per lane per round
 constexpr int kRbeWarpKeys = 32 * kRbeKeys;   // keys per warp per round
 constexpr int kRbeExperts = 2;                // experts per CTA
-constexpr int kRbePad = 0x7fffffff;           // past the end: below no expert, equal to none
+constexpr uint32_t kRbePad = 0xffffffffu;     // past the end: below no expert (see rbe_load)
 
-// v[4c + q] = key at position wb + 128c + 4*lane + q (kRbePad past n).
-__device__ __forceinline__ void rbe_load(int (&v)[kRbeKeys], const int32_t* __restrict__ idx,
-                                         int64_t wb, int lane, int64_t n, int E, bool vec_ok) {
+// v[4c + q] = raw key at position wb + 128c + 4*lane + q, or kRbePad past n;
+// returns the mask of this lane's positions below n.  Keys are not clamped:
+// compared as unsigned, a key below e0 (<= E) is a valid expert id, and a
+// key outside [0, E) falls in the sentinel bin.  A padded position equals no
+// valid id and is below no e0, and the returned mask keeps it out of the
+// sentinel bin (every 32-bit pattern is a possible key).
+__device__ __forceinline__ uint32_t rbe_load(uint32_t (&v)[kRbeKeys], const int32_t* __restrict__ idx,
+                                             int64_t wb, int lane, int64_t n, bool vec_ok) {
+  uint32_t valid = 0xffffffffu;
 #pragma unroll
   for (int c = 0; c < kRbeVecs; ++c) {
     const int64_t p = wb + 128 * c + 4 * lane;
     if (vec_ok && p + 4 <= n) {
       const int4 q = __ldg(reinterpret_cast<const int4*>(idx + p));
-      v[4 * c] = clamp_key(q.x, E);
-      v[4 * c + 1] = clamp_key(q.y, E);
-      v[4 * c + 2] = clamp_key(q.z, E);
-      v[4 * c + 3] = clamp_key(q.w, E);
+      v[4 * c] = static_cast<uint32_t>(q.x);
+      v[4 * c + 1] = static_cast<uint32_t>(q.y);
+      v[4 * c + 2] = static_cast<uint32_t>(q.z);
+      v[4 * c + 3] = static_cast<uint32_t>(q.w);
     } else {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) v[4 * c + q] = p + q < n ? clamp_key(__ldg(idx + p + q), E) : kRbePad;
+      for (int q = 0; q < 4; ++q) {
+        const bool in = p + q < n;
+        v[4 * c + q] = in ? static_cast<uint32_t>(__ldg(idx + p + q)) : kRbePad;
+        if (!in) valid &= ~(1u << (4 * c + q));
+      }
     }
   }
+  return valid;
+}
+
+// Key v falls in bin b (b < E: equal ids; b == E: any id outside [0, E);
+// b > E, a CTA's slot past the sentinel bin: nothing).  Padded positions are
+// removed from the sentinel bin by the caller's mask.
+__device__ __forceinline__ bool rbe_in_bin(uint32_t v, int b, int E) {
+  return b < E ? v == static_cast<uint32_t>(b) : (b == E && v >= static_cast<uint32_t>(E));
 }
 
 // Sum over the block of per-warp values published in s[0..nw) (after a
@@ -337,13 +355,15 @@ __global__ void __launch_bounds__(1024) route_by_expert_kernel(
   if (rounds > 1) {
     int lt = 0, eq[kRbeExperts] = {};
     for (int64_t r = 0; r < rounds; ++r) {
-      int v[kRbeKeys];
-      rbe_load(v, idx, r * per_round + static_cast<int64_t>(warp) * kRbeWarpKeys, lane, n, E, vec_ok);
+      uint32_t v[kRbeKeys];
+      const uint32_t valid =
+          rbe_load(v, idx, r * per_round + static_cast<int64_t>(warp) * kRbeWarpKeys, lane, n, vec_ok);
 #pragma unroll
       for (int i = 0; i < kRbeKeys; ++i) {
-        lt += v[i] < e0;
+        lt += v[i] < static_cast<uint32_t>(e0);
 #pragma unroll
-        for (int j = 0; j < kRbeExperts; ++j) eq[j] += v[i] == e0 + j;
+        for (int j = 0; j < kRbeExperts; ++j)
+          eq[j] += rbe_in_bin(v[i], e0 + j, E) && ((valid >> i) & 1u);
       }
     }
     lt = __reduce_add_sync(kFull, lt);
@@ -363,16 +383,19 @@ __global__ void __launch_bounds__(1024) route_by_expert_kernel(
   const unsigned lanes_below = lanemask_lt();
   for (int64_t r = 0; r < rounds; ++r) {
     const int64_t wb = r * per_round + static_cast<int64_t>(warp) * kRbeWarpKeys;
-    int v[kRbeKeys];
-    rbe_load(v, idx, wb, lane, n, E, vec_ok);
+    uint32_t v[kRbeKeys];
+    const uint32_t valid = rbe_load(v, idx, wb, lane, n, vec_ok);
     int lt = 0;
     uint32_t m[kRbeExperts] = {};
 #pragma unroll
     for (int i = 0; i < kRbeKeys; ++i) {
-      lt += v[i] < e0;
+      lt += v[i] < static_cast<uint32_t>(e0);
 #pragma unroll
-      for (int j = 0; j < kRbeExperts; ++j) m[j] |= static_cast<uint32_t>(v[i] == e0 + j) << i;
+      for (int j = 0; j < kRbeExperts; ++j)
+        m[j] |= static_cast<uint32_t>(rbe_in_bin(v[i], e0 + j, E)) << i;
     }
+#pragma unroll
+    for (int j = 0; j < kRbeExperts; ++j) m[j] &= valid;
     lt = __reduce_add_sync(kFull, lt);
     int cw[kRbeExperts];
 #pragma unroll

@@ -134,6 +134,26 @@ def test_route_vs_oracle(T, k, E, sent):
     assert np.array_equal(off.cpu().numpy(), ooff)
 
 
+@pytest.mark.parametrize("T,k,E", [(37, 3, 16), (1000, 7, 256), (4099, 8, 1023)])
+def test_route_arbitrary_invalid_keys(T, k, E):
+    """Every id outside [0, E) is the sentinel bin, whatever its bit pattern
+    (-1, -2, INT_MIN, INT_MAX, E, E + 1, ...), including in the last, partial
+    16-byte vector of keys, where padding positions must stay out of it."""
+    import layerstormexpertkernels_b200 as P
+    g = torch.Generator().manual_seed(T + k)
+    idx = torch.randint(-3, E + 3, (T, k), generator=g, dtype=torch.int32)
+    flat = idx.view(-1)
+    specials = torch.tensor([-2, -(2 ** 31), 2 ** 31 - 1, E, E + 1, -1, 0, E - 1],
+                            dtype=torch.int32)
+    flat[-len(specials):] = specials
+    flat[: len(specials)] = specials
+    off, s2d, perm = P.moe_route(idx.cuda(), E)
+    _, ooff, os2d, operm = O.moe_permute(None, idx.numpy(), E)
+    assert np.array_equal(perm.cpu().numpy(), operm)
+    assert np.array_equal(s2d.cpu().numpy(), os2d)
+    assert np.array_equal(off.cpu().numpy(), ooff)
+
+
 def test_route_unaligned_indices_and_matches_permute():
     """topk_indices that start 4 bytes past a 16-byte boundary take the
     scalar key loads; the maps equal moe_permute's."""
