@@ -7,13 +7,12 @@
 // and of the expert FFN flow in USAGE.md:40-57.
 //
 // Tiling.  A tile is 128 rows x 256 B-rows x all of K.  A work unit is one
-// n-tile of one expert against one m-tile or, when the expert has another
-// m-tile after it, against two m-tiles at once (a paired unit: M = 256 from
-// two MMAs that share every weight box, accumulating into both TMEM
-// accumulators).  Pairing halves the shared-memory fill of weight boxes for
-// experts with more than 128 rows; at DeepSeek-V3 shape (about 128 rows per
-// expert) half the experts have a short second tile, which without pairing
-// re-read the whole weight tile.  Units are (expert, n-tile, m-unit) in that
+// n-tile of one expert against: one tile of at most 128 rows; a pair of
+// full tiles (a complete 256-row block: two MMAs that share every weight
+// box, one TMEM accumulator each); or, for a remainder of 129..255 rows, one
+// wide swapped tile of all of them (below).  Every expert row therefore
+// passes through a weight stage once per n-tile, and no weight tile is
+// filled into shared memory twice for one expert.  Units are (expert, n-tile, m-unit) in that
 // nesting, m fastest, so the m-units that share one weight tile are taken by
 // neighbouring CTAs at the same time and the weight tile is read from HBM
 // once (later reads hit L2); the 16-28 n-tiles of one expert reuse its A rows
@@ -44,19 +43,22 @@
 //               global, then release the accumulator; a single unit's
 //               epilogue overlaps the next unit's main loop thanks to the
 //               second accumulator (a paired unit waits for both).
-// Small tiles (at most kSwapMaxRows valid rows: experts of at most 64 rows,
-// the last tile of an expert, whether it runs alone or as the second tile of
-// a paired unit, every tile at decode sizes) swap the operands: the two
-// weight boxes become the MMA's M side (2 x M=128) and the tile's r token
-// rows its N side (N = r rounded up to 16), so the tensor-core work scales
-// with r instead of a full 128-row tile.  At DeepSeek-V3 shape most paired
-// units are a full tile plus a few rows, and with the second tile swapped
-// the MMA holds each weight stage about half as long, so more of the ring
-// stays in flight.  Such a tile's A rows arrive as r/16 boxes of 16 rows
-// (a second tensor map) instead of one 128-row box.  The epilogue of a
-// swapped tile reads the transposed accumulator (TMEM lane = output column,
-// TMEM column = token).  The same products are summed in the same k order
-// either way.
+// Swapped tiles (small ones of at most kSwapMaxRows rows: experts of at most
+// 64 rows, a remainder of at most 64, every tile at decode sizes; and wide
+// ones of 129..255 rows) put the two weight boxes on the MMA's M side
+// (2 x M=128) and the tile's r token rows on its N side (N = r rounded up to
+// 16, at most 256).  An M=128 tcgen05.mma costs about 71 cycles for any
+// N <= 144 and runs at the dense rate only from N ~ 144 up (measured on
+// B200), so the unit kinds are chosen by MMA count: at DeepSeek-V3 shape
+// (about 128-150 rows per expert) a full tile plus a swapped tail of a few
+// rows took 4 + 8 MMAs (~1110 cycles) per k-block, more than the weights
+// take to arrive at the B200's clock under this load, while one wide tile
+// takes 8 MMAs at N ~ 144 (~580 cycles).  A swapped tile's A rows arrive as
+// 16-row boxes (a second tensor map; a wide tile's first 128 rows as one
+// box).  The epilogue of a swapped tile reads the transposed accumulator
+// (TMEM lane = output column, TMEM column = token); a wide tile's occupies
+// TMEM columns 0 .. 2N-1, both accumulators.  The same products are summed
+// in the same k order either way.
 // COMBINE mode (the expert-parallel down projection) ends each output row
 // in the combine instead of D: row p becomes bf16(w[p] * bf16(acc)) stored at
 // row dst_row[p] of rank dst_rank[p]'s combine buffer (peer memory over
@@ -353,19 +355,15 @@ __device__ __forceinline__ int mtiles_of(const S& s, int e) {
   return n > 0 ? (n + kBM - 1) / kBM : 0;
 }
 
-// Units of one n-tile of expert e: one per m-tile, or with pairing one per
-// two m-tiles (the last one alone when the count is odd).
+// Units of one n-tile of expert e.  Without pairing: one per m-tile.  With
+// pairing: one per complete 256-row block (a pair of full tiles), then one
+// for the remaining rows: a single tile when at most 128 remain, else one
+// wide swapped tile of all of them (see Unit).
 template <class S>
 __device__ __forceinline__ int munits_of(const S& s, int e, bool pairs) {
-  const int mt = mtiles_of(s, e);
-  return pairs ? (mt + 1) >> 1 : mt;
-}
-
-// Valid rows of m-tile m of expert e (1..kBM).
-template <class S>
-__device__ __forceinline__ int tile_rows(const S& s, int e, int m) {
-  const int left = s.offs[e + 1] - s.offs[e] - m * kBM;
-  return left < kBM ? left : kBM;
+  if (!pairs) return mtiles_of(s, e);
+  const int n = s.offs[e + 1] - s.offs[e];
+  return n > 0 ? (n + 2 * kBM - 1) / (2 * kBM) : 0;
 }
 
 // Instruction descriptor of a swapped tile: M=128 weight rows, N=nn tokens.
@@ -374,11 +372,21 @@ __device__ __forceinline__ uint32_t swap_idesc(int nn) {
          (static_cast<uint32_t>(kBM >> 4) << 24);
 }
 
-// A work unit: n-tile n of expert e against m-tile t0 and, when paired,
-// m-tile t0 + 1 too; both m-tiles multiply the same weight boxes.
+// A work unit: n-tile n of expert e against `rows` token rows starting at
+// m-tile t0.  Three kinds:
+//   single  one tile of at most 128 rows (swapped when at most 64)
+//   pair    two full tiles t0, t0 + 1 (256 rows) against one weight stage,
+//           one TMEM accumulator each
+//   wide    129..255 rows as one swapped tile: the two weight boxes on M and
+//           all the rows on N (rounded up to 16, at most 256), into TMEM
+//           columns 0 .. 2N-1, i.e. both accumulators.  An M=128 MMA costs
+//           about as much at N=16 as at N=144 (measured ~71 cycles, full rate
+//           only from N~144 up), so a full tile plus a swapped tail of a few
+//           rows (4 + 8 MMAs per k-block) took twice the tensor time of one
+//           wide tile (8 MMAs at N~144).
 struct Unit {
-  int e, n, t0;
-  bool pair;
+  int e, n, t0, rows;
+  bool pair, wide;
 };
 
 // Maps a unit id to its unit: the largest e with cum[e] <= id is the
@@ -399,7 +407,10 @@ __device__ __forceinline__ Unit decode_unit(const S& s, int num_experts, int id,
   u.n = local / mu;
   const int m = local - u.n * mu;
   u.t0 = pairs ? 2 * m : m;
-  u.pair = pairs && u.t0 + 1 < mtiles_of(s, lo);
+  const int left = s.offs[lo + 1] - s.offs[lo] - u.t0 * kBM;
+  u.pair = pairs && left >= 2 * kBM;
+  u.wide = pairs && !u.pair && left > kBM;
+  u.rows = u.pair ? 2 * kBM : (left < kBM || u.wide ? left : kBM);
   return u;
 }
 
@@ -411,6 +422,20 @@ __device__ __forceinline__ uint32_t tile_a_bytes(int rows, bool gathered) {
   if (!swapped) return static_cast<uint32_t>(kBM * kBK * 2);
   if (G::kSmallOnly && !gathered) return static_cast<uint32_t>(G::kABytes);
   return static_cast<uint32_t>(((rows + 15) & ~15) * kBK * 2);
+}
+
+// A bytes of a unit's stage: the first part (a0) and, for a pair, the second
+// tile's (a1; 0 otherwise).  A wide unit's rows form one part.
+template <class G>
+__device__ __forceinline__ void unit_a_bytes(const Unit& u, bool gathered, uint32_t& a0,
+                                             uint32_t& a1) {
+  if (u.pair) {
+    a0 = a1 = static_cast<uint32_t>(kBM * kBK * 2);
+    return;
+  }
+  a1 = 0u;
+  a0 = u.wide ? static_cast<uint32_t>(((u.rows + 15) & ~15) * kBK * 2)
+              : tile_a_bytes<G>(u.rows, gathered);
 }
 
 // Position in the stage ring: stage j uses record j % kRecs (barrier parity
@@ -595,18 +620,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Unit u = decode_unit(s, E, unit, pairs);
         const int row0 = s.offs[u.e] + u.t0 * kBM;
         const int brow = u.e * p.b_rows + u.n * p.b_tile_rows;
-        // A tile that runs with swapped operands needs only its rows rounded
-        // up to 16: tiled A loads them as that many 16-row boxes instead of
-        // one 128-row box.  The first tile of a paired unit is always full.
+        // A swapped tile needs only its rows rounded up to 16: tiled A loads
+        // a small tile's rows as that many 16-row boxes, and a wide unit's
+        // as one 128-row box followed by 16-row boxes for the rest.
         const bool gathered = p.gather_idx != nullptr;
-        const int rows_t0 = tile_rows(s, u.e, u.t0);
-        const int rows_t1 = u.pair ? tile_rows(s, u.e, u.t0 + 1) : 0;
-        const uint32_t a0_bytes = tile_a_bytes<G>(rows_t0, gathered);
-        const uint32_t a1_bytes = u.pair ? tile_a_bytes<G>(rows_t1, gathered) : 0u;
-        const int n16_t0 = (!G::kSmallOnly && !gathered && rows_t0 <= kSwapMaxRows)
-                               ? static_cast<int>(a0_bytes / kA16Bytes) : 0;
-        const int n16_t1 = (u.pair && rows_t1 <= kSwapMaxRows)
-                               ? static_cast<int>(a1_bytes / kA16Bytes) : 0;
+        uint32_t a0_bytes, a1_bytes;
+        unit_a_bytes<G>(u, gathered, a0_bytes, a1_bytes);
+        const bool full_box = u.pair || (!u.wide && (gathered || G::kSmallOnly || u.rows > kSwapMaxRows));
+        const int head = u.wide ? kBM : 0;  // rows in the leading 128-row box
+        const int n16 = full_box ? 0 : static_cast<int>((a0_bytes - head * kBK * 2) / kA16Bytes);
         // Gathered A: the MMA reads 128 rows (or, for a swapped small tile,
         // its rows rounded up to 16); rows past the expert repeat its first
         // row (their results are discarded).
@@ -631,21 +653,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int r = 0; r < nload; r += 4)
               tma_gather4(a0 + r * kBK * 2, &tmap_a, full, kb * kBK, s.arow[r], s.arow[r + 1],
                           s.arow[r + 2], s.arow[r + 3], pol_a);
-          } else if (n16_t0 > 0) {
-            for (int b = 0; b < n16_t0; ++b)
-              tma_load_2d(a0 + b * kA16Bytes, &tmap_a16, full, kb * kBK, row0 + 16 * b, pol_a);
           } else {
-            tma_load_2d(a0, &tmap_a, full, kb * kBK, row0, pol_a);
+            if (full_box || u.wide) tma_load_2d(a0, &tmap_a, full, kb * kBK, row0, pol_a);
+            for (int b = 0; b < n16; ++b)
+              tma_load_2d(a0 + head * kBK * 2 + b * kA16Bytes, &tmap_a16, full, kb * kBK,
+                          row0 + head + 16 * b, pol_a);
           }
-          if (u.pair) {
-            if (n16_t1 > 0) {
-              for (int b = 0; b < n16_t1; ++b)
-                tma_load_2d(s.ring + oa1 + b * kA16Bytes, &tmap_a16, full, kb * kBK,
-                            row0 + kBM + 16 * b, pol_a);
-            } else {
-              tma_load_2d(s.ring + oa1, &tmap_a, full, kb * kBK, row0 + kBM, pol_a);
-            }
-          }
+          if (u.pair) tma_load_2d(s.ring + oa1, &tmap_a, full, kb * kBK, row0 + kBM, pol_a);
           tma_load_2d(s.ring + ob0, &tmap_b, full, kb * kBK, brow, pol_w);
           tma_load_2d(s.ring + ob0 + kBoxBytes, &tmap_b, full, kb * kBK, brow + p.b_second, pol_w);
           pos.advance(span);
@@ -676,31 +690,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (unit < 0) break;
         const Unit u = decode_unit(s, E, unit, pairs);
-        const int rows_here = tile_rows(s, u.e, u.t0);
-        const bool swapped = !u.pair && (G::kSmallOnly || rows_here <= kSwapMaxRows);
-        const int nn = (rows_here + 15) & ~15;
+        const bool two = u.pair || u.wide;  // the unit takes both accumulators
+        const bool swapped = u.wide || (!u.pair && (G::kSmallOnly || u.rows <= kSwapMaxRows));
+        const int nn = (u.rows + 15) & ~15;
         const uint32_t sw_idesc = swap_idesc(nn);
-        // A pair's second tile (the expert's last) with few rows also swaps.
-        const int rows1 = u.pair ? tile_rows(s, u.e, u.t0 + 1) : 0;
-        const bool swapped1 = u.pair && rows1 <= kSwapMaxRows;
-        const int nn1 = (rows1 + 15) & ~15;
-        const uint32_t sw_idesc1 = swap_idesc(nn1);
         const int acc0 = static_cast<int>(ac & 1u);
         const int acc1 = static_cast<int>((ac + 1) & 1u);
         if (!mbar_wait(&s.acc_empty_bar[acc0], ((ac >> 1) & 1u) ^ 1u, abort, kDevErrGemmMmaWait,
                        true) ||
-            (u.pair && !mbar_wait(&s.acc_empty_bar[acc1], (((ac + 1) >> 1) & 1u) ^ 1u, abort,
-                                  kDevErrGemmMmaWait, true))) {
+            (two && !mbar_wait(&s.acc_empty_bar[acc1], (((ac + 1) >> 1) & 1u) ^ 1u, abort,
+                               kDevErrGemmMmaWait, true))) {
           ok = false;
           break;
         }
-        ac += u.pair ? 2u : 1u;
+        ac += two ? 2u : 1u;
         tc_fence_after();
-        const uint32_t d0 = tmem_base + static_cast<uint32_t>(acc0 * kBN);
+        // A wide tile spans TMEM columns 0 .. 2nn-1 (both accumulators).
+        const uint32_t d0 = tmem_base + (u.wide ? 0u : static_cast<uint32_t>(acc0 * kBN));
         const uint32_t d1 = tmem_base + static_cast<uint32_t>(acc1 * kBN);
         const bool gathered = p.gather_idx != nullptr;
-        const uint32_t a0_bytes = tile_a_bytes<G>(rows_here, gathered);
-        const uint32_t a1_bytes = u.pair ? tile_a_bytes<G>(rows1, gathered) : 0u;
+        uint32_t a0_bytes, a1_bytes;
+        unit_a_bytes<G>(u, gathered, a0_bytes, a1_bytes);
         for (int kb = 0; kb < p.num_kb; ++kb) {
           const int rec = pos.rec();
           if (!mbar_wait(&s.full_bar[rec], pos.parity(), abort, kDevErrGemmMmaWait, true)) {
@@ -730,16 +740,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < kBK / 16; ++kk)
               umma_bf16(d0, smem_desc_sw128(a0_addr + kk * 32), smem_desc_sw128(b0_addr + kk * 32),
                         kIdesc, (kb | kk) != 0 ? 1u : 0u);
-            if (swapped1) {
-#pragma unroll
-              for (int kk = 0; kk < kBK / 16; ++kk) {
-                const uint64_t tok = smem_desc_sw128(a1_addr + kk * 32);
-                const uint32_t acc_in = (kb | kk) != 0 ? 1u : 0u;
-                umma_bf16(d1, smem_desc_sw128(b0_addr + kk * 32), tok, sw_idesc1, acc_in);
-                umma_bf16(d1 + static_cast<uint32_t>(nn1), smem_desc_sw128(b1_addr + kk * 32), tok,
-                          sw_idesc1, acc_in);
-              }
-            } else if (u.pair) {
+            if (u.pair) {
 #pragma unroll
               for (int kk = 0; kk < kBK / 16; ++kk)
                 umma_bf16(d1, smem_desc_sw128(a1_addr + kk * 32),
@@ -751,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok) {
           umma_commit(&s.acc_full_bar[acc0]);
-          if (u.pair) umma_commit(&s.acc_full_bar[acc1]);
+          if (two) umma_commit(&s.acc_full_bar[acc1]);
         }
       }
       // Outstanding MMAs read shared memory and write TMEM: finish them first.
@@ -781,6 +782,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (unit < 0) break;
       const Unit u = decode_unit(s, E, unit, pairs);
       const int e = u.e;
+      // A wide tile fills both accumulators: wait for the second one too.
+      if (u.wide && !mbar_wait(&s.acc_full_bar[(ac + 1) & 1u], ((ac + 1) >> 1) & 1u, abort,
+                               kDevErrGemmEpilogueWait, true))
+        break;
       for (int ti = 0; ti < (u.pair ? 2 : 1); ++ti, ++ac) {
         const int acc = static_cast<int>(ac & 1u);
         if (!mbar_wait(&s.acc_full_bar[acc], (ac >> 1) & 1u, abort, kDevErrGemmEpilogueWait,
@@ -790,13 +795,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const int m = u.t0 + ti;
-        const int rows_here = tile_rows(s, e, m);
-        const bool swapped = G::kSmallOnly || rows_here <= kSwapMaxRows;
+        const int rows_here = u.pair ? kBM : u.rows;
+        const bool swapped = u.wide || G::kSmallOnly || rows_here <= kSwapMaxRows;
         const int row0 = s.offs[e] + m * kBM;
         const int r = row0 + q * 32 + lane;
         const bool valid = r < s.offs[e + 1];
-        const uint32_t tbase =
-            tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kBN);
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                               (u.wide ? 0u : static_cast<uint32_t>(acc * kBN));
         const int col0 = u.n * p.out_tile_cols;
         const int cols_here = min(p.out_tile_cols, p.n_out - col0);
         __nv_bfloat16* drow = nullptr;
@@ -912,7 +917,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s.acc_empty_bar[acc]);
+        if (lane == 0) {
+          mbar_arrive(&s.acc_empty_bar[acc]);
+          if (u.wide) mbar_arrive(&s.acc_empty_bar[(ac + 1) & 1u]);
+        }
+        if (u.wide) ++ac;
       }
     }
   }

@@ -163,15 +163,16 @@ def test_tile_shape_does_not_change_results(swiglu):
 @pytest.mark.parametrize("swiglu", [False, True])
 @pytest.mark.parametrize("K", [64, 576, 1024])
 def test_paired_tiles_match_single_tiles(swiglu, K):
-    """Experts with more than 128 rows run their m-tiles two at a time
-    against one weight tile (two accumulators); the rows must come out
-    bit-identical to the same rows computed one 128-row tile per expert.
-    The k-block counts (1, 9, 16) move the shared-memory ring's wrap point
-    through every box position."""
+    """Experts with more than 128 rows run each complete 256-row block as a
+    paired unit (two accumulators against one weight tile) and a remainder
+    of 129..255 rows as one wide swapped tile (N up to 256); the rows must
+    come out bit-identical to the same rows computed one 128-row tile per
+    expert.  The k-block counts (1, 9, 16) move the shared-memory ring's
+    wrap point through every box position."""
     N = 512
     g = torch.Generator().manual_seed(K + swiglu)
     b = (torch.randn(1, N, K, generator=g) / np.sqrt(K)).to(torch.bfloat16).cuda()
-    for rows in (129, 200, 256, 257, 300, 384, 520):
+    for rows in (129, 200, 255, 256, 257, 300, 384, 400, 511, 520):
         a = torch.randn(rows, K, generator=g).to(torch.bfloat16).cuda()
         off = torch.tensor([0, rows], dtype=torch.int32, device="cuda")
         cuts = list(range(0, rows, 128)) + [rows]
@@ -188,7 +189,7 @@ def test_paired_tiles_match_single_tiles(swiglu, K):
 
 
 def test_tail_tiles_of_large_experts():
-    # Experts with 129..192 rows: a full tile paired with a short one.
+    # Experts with 129..192 rows: one wide swapped tile each.
     a, b, off = make_problem([130, 192, 150, 129], 512, 256, seed=21)
     out = ek().grouped_gemm_bf16(a.cuda(), b.cuda(), off.cuda())
     sync_and_check_device_error()

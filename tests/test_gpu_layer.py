@@ -82,22 +82,25 @@ def test_layer_deepseek_shape_sampled(deepseek_weights, T, sample):
     assert_layer_close(out[torch.as_tensor(toks).cuda()], np.concatenate(refs))
 
 
-# Experts with crafted row counts at cfg1 and the GEMM tile class each one
-# exercises (tiles are 128 rows; consecutive m-tiles of an expert pair up;
-# an unpaired tile of <= 64 rows runs with swapped operands).
+# Experts with crafted row counts at cfg1 and the GEMM unit kinds each one
+# exercises (tiles are 128 rows; complete 256-row blocks run as paired
+# units; a remainder of at most 128 rows is one tile, swapped when at most
+# 64; a remainder of 129..255 rows is one wide swapped tile).
 TILE_CLASS_COUNTS = {
     3: 1,       # one swapped tile, one valid row
     9: 64,      # one swapped tile, full swap width
-    17: 65,     # one unswapped unpaired tile, 65 valid rows
-    30: 128,    # one full unpaired tile
-    33: 129,    # a paired unit whose second tile has one row
+    12: 255,    # one wide swapped tile at the largest width (N = 256)
+    17: 65,     # one unswapped tile, 65 valid rows
+    30: 128,    # one full tile
+    33: 129,    # one wide swapped tile of 129 rows (N = 144)
     40: 256,    # a paired unit of two full tiles
-    47: 300,    # a paired unit + an unpaired swapped tail of 44 rows
-    55: 356,    # a paired unit + an unpaired unswapped tail of 100 rows
-    62: 1100,   # the heaviest expert: four paired units + an unpaired 76-row tail
+    47: 300,    # a paired unit + a swapped tail of 44 rows
+    50: 400,    # a paired unit + a wide tail of 144 rows
+    55: 356,    # a paired unit + an unswapped tail of 100 rows
+    62: 1100,   # the heaviest expert: four paired units + a 76-row tail
 }
 # Partners for the probe tokens' remaining slots (groups 2 and 3), so the
-# oracle needs the weights of only these 17 experts.
+# oracle needs the weights of only these and the special experts.
 PROBE_MATES = (69, 78, 87, 95, 98, 107, 116, 125)
 
 
@@ -151,10 +154,11 @@ def craft_tile_class_routing(T=4096, E=256, k=8, n_group=8, seed=11):
 
 def test_layer_cfg1_every_tile_class_vs_oracle(deepseek_weights):
     """cfg1 layer (T=4096) on crafted logits: experts with 1, 64, 65, 128,
-    129, 256, 300, 356 and 1100 rows, so every GEMM tile class of both
-    projections occurs (swapped small tiles, unpaired tiles, paired units with
-    full and one-row second tiles, unpaired tails above and below the swap
-    width, the heaviest expert's tail).  The tokens sitting at every
+    129, 255, 256, 300, 356, 400 and 1100 rows, so every GEMM unit kind of
+    both projections occurs (swapped small tiles, single full and partial
+    tiles, wide swapped tiles from N=144 to N=256 alone and after a pair,
+    paired units, tails above and below the swap width, the heaviest
+    expert's tail).  The tokens sitting at every
     tile-boundary row of those experts are checked in full against the oracle
     (all 7168 columns cross every n-tile of the down projection)."""
     from layerstormexpertkernels_b200.synthetic import token_inputs
