@@ -142,8 +142,14 @@ struct Geom {
   static_assert(RING_BYTES >= 2 * kBoxBytes + 2 * kABytes, "the largest stage fits the ring");
   static_assert(kRecs * kMinStageBytes > RING_BYTES, "a record is reused only after its stage left");
 };
-// Any routing: a 208 KB ring, four to six stages in flight.
-using GeomFull = Geom<13 * kBoxBytes, 128, kMaxExperts>;
+// Up to 256 experts (DeepSeek-V3 and smaller): the unit table takes 2 KB of
+// shared memory and the ring the rest, 223 KB.  The ring is the kernel's
+// main lever: at cfg1 it holds the weight bytes in flight while the MMA
+// works through landed stages (a 176 KB ring measured 13 % slower than
+// 208 KB).
+using GeomFull = Geom<223 * 1024, 128, 256>;
+// Up to 1024 experts: an 8 KB unit table and a 208 KB ring.
+using GeomFullWide = Geom<13 * kBoxBytes, 128, kMaxExperts>;
 // Decode (every expert has at most 32 rows): a 4 KB token box, six 36 KB
 // stages in flight.
 using GeomDecode = Geom<6 * (4096 + 2 * kBoxBytes), 32, 256>;
@@ -213,6 +219,7 @@ constexpr size_t smem_bytes() {
   return sizeof(SmemT<G>) + 1024;
 }
 static_assert(smem_bytes<GeomFull>() <= 227 * 1024, "shared memory budget");
+static_assert(smem_bytes<GeomFullWide>() <= 227 * 1024, "shared memory budget");
 static_assert(smem_bytes<GeomDecode>() <= 227 * 1024, "shared memory budget");
 
 // ---- PTX wrappers ----------------------------------------------------------
@@ -1062,8 +1069,11 @@ lsek_status launch(void* D, const void* A, const void* B, const int32_t* offsets
   if (bound >= 0 && bound <= kDecodeMaxRows && E <= GeomDecode::kMaxE)
     return launch_geom<MODE, GeomDecode>(D, A, B, offsets, E, rows, n_out, b_rows, K, limit,
                                          counter, st, combine, gather);
-  return launch_geom<MODE, GeomFull>(D, A, B, offsets, E, rows, n_out, b_rows, K, limit, counter,
-                                     st, combine, gather);
+  if (E <= GeomFull::kMaxE)
+    return launch_geom<MODE, GeomFull>(D, A, B, offsets, E, rows, n_out, b_rows, K, limit,
+                                       counter, st, combine, gather);
+  return launch_geom<MODE, GeomFullWide>(D, A, B, offsets, E, rows, n_out, b_rows, K, limit,
+                                         counter, st, combine, gather);
 }
 
 lsek_status validate(const char* name, const void* D, const void* A, const void* B,
