@@ -7,12 +7,11 @@
 // and of the expert FFN flow in USAGE.md:40-57.
 //
 // Tiling.  A tile is 128 rows x 256 B-rows x all of K.  A work unit is one
-// n-tile of one expert against: one tile of at most 128 rows; a pair of
-// full tiles (a complete 256-row block: two MMAs that share every weight
-// box, one TMEM accumulator each); or, for a remainder of 129..255 rows, one
-// wide swapped tile of all of them (below).  Every expert row therefore
-// passes through a weight stage once per n-tile, and no weight tile is
-// filled into shared memory twice for one expert.  Units are (expert, n-tile, m-unit) in that
+// n-tile of one expert against: a pair of tiles (up to 256 rows: two MMAs
+// that share every weight box, one TMEM accumulator each); one wide swapped
+// tile of 129..192 rows (below); or one tile of at most 128 rows.  Every
+// expert row passes through a weight stage once per n-tile, and no weight
+// tile is filled into shared memory twice for one expert.  Units are (expert, n-tile, m-unit) in that
 // nesting, m fastest, so the m-units that share one weight tile are taken by
 // neighbouring CTAs at the same time and the weight tile is read from HBM
 // once (later reads hit L2); the 16-28 n-tiles of one expert reuse its A rows
@@ -43,19 +42,18 @@
 //               global, then release the accumulator; a single unit's
 //               epilogue overlaps the next unit's main loop thanks to the
 //               second accumulator (a paired unit waits for both).
-// Swapped tiles (small ones of at most kSwapMaxRows rows: experts of at most
-// 64 rows, a remainder of at most 64, every tile at decode sizes; and wide
-// ones of 129..255 rows) put the two weight boxes on the MMA's M side
-// (2 x M=128) and the tile's r token rows on its N side (N = r rounded up to
-// 16, at most 256).  An M=128 tcgen05.mma costs about 71 cycles for any
-// N <= 144 and runs at the dense rate only from N ~ 144 up (measured on
-// B200), so the unit kinds are chosen by MMA count: at DeepSeek-V3 shape
-// (about 128-150 rows per expert) a full tile plus a swapped tail of a few
-// rows took 4 + 8 MMAs (~1110 cycles) per k-block, more than the weights
-// take to arrive at the B200's clock under this load, while one wide tile
-// takes 8 MMAs at N ~ 144 (~580 cycles).  A swapped tile's A rows arrive as
-// 16-row boxes (a second tensor map; a wide tile's first 128 rows as one
-// box).  The epilogue of a swapped tile reads the transposed accumulator
+// Swapped tiles (wide ones of 129..192 rows; small ones of at most
+// kSwapMaxRows rows at decode sizes and with a gathered A) put the two
+// weight boxes on the MMA's M side (2 x M=128) and the tile's r token rows
+// on its N side (N = r rounded up to 16).  An M=128 tcgen05.mma costs about
+// 71 cycles for any N <= 144 and runs at the dense rate only from N ~ 144 up
+// (measured on B200), so the unit kinds are chosen by MMA count: at
+// DeepSeek-V3 shape (about 128-150 rows per expert) a full tile plus a
+// swapped tail of a few rows took 4 + 8 MMAs (~1110 cycles) per k-block,
+// more than the weights take to arrive at the B200's clock under this load
+// (1.5-1.6 GHz measured), while one wide tile takes 8 MMAs at N ~ 144 (~580
+// cycles).  A wide tile's A rows arrive as one 128-row box and 16-row boxes
+// (a second tensor map).  The epilogue of a swapped tile reads the transposed accumulator
 // (TMEM lane = output column, TMEM column = token); a wide tile's occupies
 // TMEM columns 0 .. 2N-1, both accumulators.  The same products are summed
 // in the same k order either way.
@@ -108,6 +106,7 @@ constexpr int kMaxExperts = 1024;
 constexpr int kUnitQ = 4;                      // unit ids in flight between warps
 constexpr int kSwapMaxRows = 64;               // tiles this small use swapped operands
 constexpr int kA16Bytes = 16 * kBK * 2;        // one 16-row A box (2 KB)
+constexpr int kWideMaxRows = 192;              // remainders of 129..192 rows run as wide tiles
 
 // Pipeline geometry.  Each k-block of a unit is one stage: two 128-row
 // weight boxes (adjacent, one N=256 MMA reads both) and the A rows of its
@@ -363,9 +362,8 @@ __device__ __forceinline__ int mtiles_of(const S& s, int e) {
 }
 
 // Units of one n-tile of expert e.  Without pairing: one per m-tile.  With
-// pairing: one per complete 256-row block (a pair of full tiles), then one
-// for the remaining rows: a single tile when at most 128 remain, else one
-// wide swapped tile of all of them (see Unit).
+// pairing: one per 256-row block and one for the remaining rows (see
+// decode_unit for how the last rows are cut).
 template <class S>
 __device__ __forceinline__ int munits_of(const S& s, int e, bool pairs) {
   if (!pairs) return mtiles_of(s, e);
@@ -380,17 +378,19 @@ __device__ __forceinline__ uint32_t swap_idesc(int nn) {
 }
 
 // A work unit: n-tile n of expert e against `rows` token rows starting at
-// m-tile t0.  Three kinds:
-//   single  one tile of at most 128 rows (swapped when at most 64)
-//   pair    two full tiles t0, t0 + 1 (256 rows) against one weight stage,
-//           one TMEM accumulator each
-//   wide    129..255 rows as one swapped tile: the two weight boxes on M and
-//           all the rows on N (rounded up to 16, at most 256), into TMEM
-//           columns 0 .. 2N-1, i.e. both accumulators.  An M=128 MMA costs
-//           about as much at N=16 as at N=144 (measured ~71 cycles, full rate
-//           only from N~144 up), so a full tile plus a swapped tail of a few
-//           rows (4 + 8 MMAs per k-block) took twice the tensor time of one
-//           wide tile (8 MMAs at N~144).
+// m-tile t0.  Three kinds (decode_unit cuts an expert's rows into them):
+//   pair    tiles t0 and t0 + 1 (193..256 rows; the second may be partial)
+//           against one weight stage, one TMEM accumulator each
+//   wide    129..192 rows as one swapped tile: the two weight boxes on M and
+//           all the rows on N (rounded up to 16), into TMEM columns
+//           0 .. 2N-1, i.e. both accumulators.  An M=128 MMA costs about as
+//           much at N=16 as at N=144 (measured ~71 cycles, the dense rate
+//           only from N~144 up), so this takes 8 MMAs at N~144-192
+//           (~580-770 cycles a k-block) where a full tile plus a swapped tail
+//           took 4 + 8 (~1110) and a pair 8 at N=256 (~1024); above 192 rows
+//           a pair costs no more and keeps the faster unswapped epilogue
+//   single  at most 128 rows: one tile, swapped only where single_swapped
+//           says so
 struct Unit {
   int e, n, t0, rows;
   bool pair, wide;
@@ -413,20 +413,53 @@ __device__ __forceinline__ Unit decode_unit(const S& s, int num_experts, int id,
   const int mu = munits_of(s, lo, pairs);
   u.n = local / mu;
   const int m = local - u.n * mu;
-  u.t0 = pairs ? 2 * m : m;
-  const int left = s.offs[lo + 1] - s.offs[lo] - u.t0 * kBM;
-  u.pair = pairs && left >= 2 * kBM;
-  u.wide = pairs && !u.pair && left > kBM;
-  u.rows = u.pair ? 2 * kBM : (left < kBM || u.wide ? left : kBM);
+  const int n = s.offs[lo + 1] - s.offs[lo];
+  u.pair = u.wide = false;
+  if (!pairs) {
+    u.t0 = m;
+    u.rows = min(n - m * kBM, kBM);
+    return u;
+  }
+  // 256-row blocks run as pairs.  When at most 64 rows follow the last
+  // block, its second half and those rows run as one wide tile instead
+  // (128 + r rows): a full tile + a wide tile cost 4 + 8 MMAs at N >= 144 per
+  // k-block, a pair plus a tile of r rows 8 + 4 at N = 256.
+  const int nb = n / (2 * kBM), r = n - nb * 2 * kBM;
+  const bool split = r > 0 && r <= kSwapMaxRows && nb >= 1;
+  const int full_pairs = nb - (split ? 1 : 0);
+  if (m < full_pairs) {
+    u.t0 = 2 * m;
+    u.pair = true;
+    u.rows = 2 * kBM;
+  } else if (split) {
+    u.t0 = 2 * full_pairs + (m - full_pairs);
+    u.wide = m > full_pairs;
+    u.rows = u.wide ? kBM + r : kBM;
+  } else {
+    u.t0 = 2 * m;
+    const int left = n - u.t0 * kBM;
+    u.pair = left > kWideMaxRows;
+    u.wide = !u.pair && left > kBM;
+    u.rows = u.pair ? min(left, 2 * kBM) : left;
+  }
   return u;
 }
 
-// A bytes of one tile in a stage: a full tile's 128-row box, the tiled box
-// of the decode geometry, or a swapped tile's rows rounded up to 16.
+// Whether a single tile runs with swapped operands: in the decode geometry,
+// and for a gathered A of at most kSwapMaxRows rows (a full tile would
+// gather 128 rows per k-block).  A tiled single tile always runs unswapped:
+// its four N=256 MMAs (~512 cycles a k-block) cost less than a swapped
+// tile's eight (~570-780 cycles measured), whatever its row count.
+template <class G>
+__device__ __forceinline__ bool single_swapped(int rows, bool gathered) {
+  return G::kSmallOnly || (gathered && rows <= kSwapMaxRows);
+}
+
+// A bytes of one single tile in a stage: a full tile's 128-row box, the
+// tiled box of the decode geometry, or a swapped tile's rows rounded up to 16.
 template <class G>
 __device__ __forceinline__ uint32_t tile_a_bytes(int rows, bool gathered) {
-  const bool swapped = G::kSmallOnly || rows <= kSwapMaxRows;
-  if (!swapped) return static_cast<uint32_t>(kBM * kBK * 2);
+  if (!single_swapped<G>(rows, gathered)) return static_cast<uint32_t>(kBM * kBK * 2);
   if (G::kSmallOnly && !gathered) return static_cast<uint32_t>(G::kABytes);
   return static_cast<uint32_t>(((rows + 15) & ~15) * kBK * 2);
 }
@@ -633,9 +666,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool gathered = p.gather_idx != nullptr;
         uint32_t a0_bytes, a1_bytes;
         unit_a_bytes<G>(u, gathered, a0_bytes, a1_bytes);
-        const bool full_box = u.pair || (!u.wide && (gathered || G::kSmallOnly || u.rows > kSwapMaxRows));
-        const int head = u.wide ? kBM : 0;  // rows in the leading 128-row box
-        const int n16 = full_box ? 0 : static_cast<int>((a0_bytes - head * kBK * 2) / kA16Bytes);
+        // A wide unit's rows: one 128-row box, then 16-row boxes.
+        const int n16 = u.wide ? static_cast<int>((a0_bytes - kBM * kBK * 2) / kA16Bytes) : 0;
         // Gathered A: the MMA reads 128 rows (or, for a swapped small tile,
         // its rows rounded up to 16); rows past the expert repeat its first
         // row (their results are discarded).
@@ -661,10 +693,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_gather4(a0 + r * kBK * 2, &tmap_a, full, kb * kBK, s.arow[r], s.arow[r + 1],
                           s.arow[r + 2], s.arow[r + 3], pol_a);
           } else {
-            if (full_box || u.wide) tma_load_2d(a0, &tmap_a, full, kb * kBK, row0, pol_a);
+            tma_load_2d(a0, &tmap_a, full, kb * kBK, row0, pol_a);
             for (int b = 0; b < n16; ++b)
-              tma_load_2d(a0 + head * kBK * 2 + b * kA16Bytes, &tmap_a16, full, kb * kBK,
-                          row0 + head + 16 * b, pol_a);
+              tma_load_2d(a0 + kBM * kBK * 2 + b * kA16Bytes, &tmap_a16, full, kb * kBK,
+                          row0 + kBM + 16 * b, pol_a);
           }
           if (u.pair) tma_load_2d(s.ring + oa1, &tmap_a, full, kb * kBK, row0 + kBM, pol_a);
           tma_load_2d(s.ring + ob0, &tmap_b, full, kb * kBK, brow, pol_w);
@@ -698,7 +730,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (unit < 0) break;
         const Unit u = decode_unit(s, E, unit, pairs);
         const bool two = u.pair || u.wide;  // the unit takes both accumulators
-        const bool swapped = u.wide || (!u.pair && (G::kSmallOnly || u.rows <= kSwapMaxRows));
+        const bool gathered = p.gather_idx != nullptr;
+        const bool swapped = u.wide || (!u.pair && single_swapped<G>(u.rows, gathered));
         const int nn = (u.rows + 15) & ~15;
         const uint32_t sw_idesc = swap_idesc(nn);
         const int acc0 = static_cast<int>(ac & 1u);
@@ -715,7 +748,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // A wide tile spans TMEM columns 0 .. 2nn-1 (both accumulators).
         const uint32_t d0 = tmem_base + (u.wide ? 0u : static_cast<uint32_t>(acc0 * kBN));
         const uint32_t d1 = tmem_base + static_cast<uint32_t>(acc1 * kBN);
-        const bool gathered = p.gather_idx != nullptr;
         uint32_t a0_bytes, a1_bytes;
         unit_a_bytes<G>(u, gathered, a0_bytes, a1_bytes);
         for (int kb = 0; kb < p.num_kb; ++kb) {
@@ -802,8 +834,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const int m = u.t0 + ti;
-        const int rows_here = u.pair ? kBM : u.rows;
-        const bool swapped = u.wide || G::kSmallOnly || rows_here <= kSwapMaxRows;
+        const int rows_here = u.pair ? min(kBM, u.rows - ti * kBM) : u.rows;
+        const bool swapped = u.wide || (!u.pair && single_swapped<G>(rows_here, p.gather_idx != nullptr));
         const int row0 = s.offs[e] + m * kBM;
         const int r = row0 + q * 32 + lane;
         const bool valid = r < s.offs[e + 1];

@@ -140,8 +140,9 @@ def test_empty_problem():
 @pytest.mark.parametrize("swiglu", [False, True])
 def test_tile_shape_does_not_change_results(swiglu):
     """A row's output must not depend on how many other rows share its
-    expert: tiles of at most 64 rows run with swapped MMA operands, full
-    tiles without, and both must give the same bits.  Expert parallelism
+    expert: calls of at most 32 rows run the decode geometry (swapped MMA
+    operands, weights on M), larger ones unswapped tiles, and both must give
+    the same bits.  Expert parallelism
     relies on this (an expert's rows are grouped differently on each rank)."""
     K, N = 1024, 512
     g = torch.Generator().manual_seed(99)
@@ -163,16 +164,18 @@ def test_tile_shape_does_not_change_results(swiglu):
 @pytest.mark.parametrize("swiglu", [False, True])
 @pytest.mark.parametrize("K", [64, 576, 1024])
 def test_paired_tiles_match_single_tiles(swiglu, K):
-    """Experts with more than 128 rows run each complete 256-row block as a
-    paired unit (two accumulators against one weight tile) and a remainder
-    of 129..255 rows as one wide swapped tile (N up to 256); the rows must
-    come out bit-identical to the same rows computed one 128-row tile per
-    expert.  The k-block counts (1, 9, 16) move the shared-memory ring's
-    wrap point through every box position."""
+    """Experts with more than 128 rows run as paired units (two
+    accumulators against one weight tile, up to 256 rows), wide swapped
+    tiles of 129..192 rows (N up to 192), and, when at most 64 rows follow a
+    256-row block, a full tile and a wide tile in place of that block; the
+    rows must come out bit-identical to the same rows computed one 128-row
+    tile per expert.  The k-block counts (1, 9, 16) move the shared-memory
+    ring's wrap point through every box position."""
     N = 512
     g = torch.Generator().manual_seed(K + swiglu)
     b = (torch.randn(1, N, K, generator=g) / np.sqrt(K)).to(torch.bfloat16).cuda()
-    for rows in (129, 200, 255, 256, 257, 300, 384, 400, 511, 520):
+    for rows in (129, 192, 193, 200, 255, 256, 257, 300, 320, 321, 384, 400, 448, 449, 511,
+                 520, 577):
         a = torch.randn(rows, K, generator=g).to(torch.bfloat16).cuda()
         off = torch.tensor([0, rows], dtype=torch.int32, device="cuda")
         cuts = list(range(0, rows, 128)) + [rows]

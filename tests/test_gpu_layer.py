@@ -83,21 +83,25 @@ def test_layer_deepseek_shape_sampled(deepseek_weights, T, sample):
 
 
 # Experts with crafted row counts at cfg1 and the GEMM unit kinds each one
-# exercises (tiles are 128 rows; complete 256-row blocks run as paired
-# units; a remainder of at most 128 rows is one tile, swapped when at most
-# 64; a remainder of 129..255 rows is one wide swapped tile).
+# exercises (tiles are 128 rows; 256-row blocks run as paired units; the
+# rows after them: more than 192 as a pair of up to 256, 129..192 as one
+# wide swapped tile, at most 128 as one tile; at most 64 rows after a block
+# turn that block's second half and them into one wide tile).
 TILE_CLASS_COUNTS = {
-    3: 1,       # one swapped tile, one valid row
-    9: 64,      # one swapped tile, full swap width
-    12: 255,    # one wide swapped tile at the largest width (N = 256)
-    17: 65,     # one unswapped tile, 65 valid rows
+    3: 1,       # one tile with one valid row
+    5: 520,     # a paired unit, a full tile and a wide tile of 136 rows
+    9: 64,      # one tile of 64 rows
+    12: 255,    # a paired unit whose second tile has 127 rows
+    17: 65,     # one tile of 65 rows
+    25: 192,    # one wide swapped tile at its largest width (N = 192)
+    26: 193,    # a paired unit whose second tile has 65 rows
     30: 128,    # one full tile
     33: 129,    # one wide swapped tile of 129 rows (N = 144)
     40: 256,    # a paired unit of two full tiles
-    47: 300,    # a paired unit + a swapped tail of 44 rows
-    50: 400,    # a paired unit + a wide tail of 144 rows
-    55: 356,    # a paired unit + an unswapped tail of 100 rows
-    62: 1100,   # the heaviest expert: four paired units + a 76-row tail
+    47: 300,    # a full tile + a wide tile of 172 rows
+    50: 400,    # a paired unit + a wide tile of 144 rows
+    55: 356,    # a paired unit + a 100-row tile
+    62: 1100,   # the heaviest expert: four paired units + a 76-row tile
 }
 # Partners for the probe tokens' remaining slots (groups 2 and 3), so the
 # oracle needs the weights of only these and the special experts.
@@ -154,11 +158,11 @@ def craft_tile_class_routing(T=4096, E=256, k=8, n_group=8, seed=11):
 
 def test_layer_cfg1_every_tile_class_vs_oracle(deepseek_weights):
     """cfg1 layer (T=4096) on crafted logits: experts with 1, 64, 65, 128,
-    129, 255, 256, 300, 356, 400 and 1100 rows, so every GEMM unit kind of
-    both projections occurs (swapped small tiles, single full and partial
-    tiles, wide swapped tiles from N=144 to N=256 alone and after a pair,
-    paired units, tails above and below the swap width, the heaviest
-    expert's tail).  The tokens sitting at every
+    129, 192, 193, 255, 256, 300, 356, 400, 520 and 1100 rows, so every GEMM
+    unit kind of both projections occurs (single full and partial tiles,
+    wide swapped tiles from N=144 to N=192 alone, after a pair and after a
+    split block, paired units with full and partial second tiles, the
+    heaviest expert's tail).  The tokens sitting at every
     tile-boundary row of those experts are checked in full against the oracle
     (all 7168 columns cross every n-tile of the down projection)."""
     from layerstormexpertkernels_b200.synthetic import token_inputs
