@@ -763,6 +763,16 @@ def run_ep(args):
                               lambda v: reduce(v, MAX))
 
     ep_combine = ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier, domain)
+    # The other transport's cfg3 numbers on the same ranks, for comparison.
+    ep_combine_other = None
+    if world > 1:
+        other = None if peer else EP.PeerDomain(CFG3_TOKENS, HIDDEN, TOPK)
+        try:
+            ep_combine_other = ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM,
+                                                barrier, other)
+        finally:
+            if other is not None:
+                other.close()
 
     plan = 1 + route_launches(T * world) + 1
     permute = route_launches(recv_rows * TOPK) + 1
@@ -806,6 +816,7 @@ def run_ep(args):
                 "roofline": roofline,
                 "stages_rank0_ms": stage_ms,
                 "ep_combine": ep_combine,
+                "ep_combine_other_transport": ep_combine_other,
                 "clocks": sampler.summary()}
         print(json.dumps(line), flush=True)
     if domain is not None:
@@ -865,10 +876,13 @@ def ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier, domai
     barrier()
     st = mean_stages(marks)
     if domain is not None:
+        # The peer combine is pushed and reduced in token chunks: its waits
+        # run inside the reduce stream, so "ep_combine_push" is the pushes and
+        # "ep_combine_reduce" the reduce work left after the last push.
         disp_names = ("ep_plan", "ep_dispatch_push", "ep_dispatch_wait", "ep_expert_permute")
-        comb_names = ("ep_combine_push", "ep_combine_wait", "ep_combine_reduce")
+        comb_names = ("ep_combine_push", "ep_combine_reduce")
         disp_x = st["ep_dispatch_push"] + st["ep_dispatch_wait"]
-        comb_x = st["ep_combine_push"] + st["ep_combine_wait"]
+        comb_x = st["ep_combine_push"]
     else:
         disp_names = ("ep_plan", "ep_dispatch_pack", "ep_dispatch_exchange", "ep_expert_permute")
         comb_names = ("ep_combine_pack", "ep_combine_exchange", "ep_combine_reduce")
@@ -893,7 +907,8 @@ def ep_combine_bench(args, dev, E, world, rank, reduce, MAX, SUM, barrier, domai
     return {"workload": (f"cfg3: T={T} tokens per rank, E={E} over {world} rank(s), H={HIDDEN} "
                          "bf16, top-8 sigmoid routing (8 groups / 4 kept), synthetic bf16 expert "
                          "outputs, weighted per-slot combine with fp32 accumulation"),
-            "transport": "peer" if domain is not None else "nccl",
+            "transport": ("peer (token-chunked: %d chunks)" % domain.combine_chunks
+                          if domain is not None else "nccl all_to_all_single"),
             "stages_ms": st,
             "steps": steps,
             "dispatch_ms": disp, "combine_ms": comb,

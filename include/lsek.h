@@ -392,8 +392,9 @@ LSEK_API lsek_status lsek_ep_dispatch_push(lsek_ep_domain* d, int32_t* send_ids,
 LSEK_API lsek_status lsek_copy_to_mapped_host(void* host_dst, const void* dev_src, size_t bytes,
                                               void* stream);
 /* Waits on the stream until every rank has published `epoch` for the
- * dispatch (what = 0) or the combine (what = 1); gives up after timeout_ns
- * (<= 0: 2 s) and records a device error. */
+ * dispatch (what = 0), the combine (what = 1) or chunk c of a token-chunked
+ * combine (what = 2 + c, c < 16); gives up after timeout_ns (<= 0: 2 s) and
+ * records a device error. */
 LSEK_API lsek_status lsek_ep_wait(lsek_ep_domain* d, int32_t what, uint32_t epoch,
                          int64_t timeout_ns, void* stream);
 /* Per permuted row of the received slots: the source rank, the row of its
@@ -416,6 +417,33 @@ LSEK_API lsek_status lsek_ep_combine_push(lsek_ep_domain* d, const void* expert_
                                  const float* dst_w, int32_t rows, const int32_t* row_lo,
                                  const int32_t* row_hi, int32_t publish, uint32_t epoch,
                                  void* stream);
+/* Token-chunked combine, step 1: chunk_of[p] = (source token of permuted
+ * row p's received row) / chunk_tokens, capped at chunks - 1, for every
+ * valid received slot (the same p as lsek_ep_combine_plan's).  Every rank
+ * must use the same chunk_tokens and chunks (e.g. from the domain's
+ * max_tokens), so chunk c of every source covers the same token range.
+ * chunks in [1, 16].  No counterpart in the reference. */
+LSEK_API lsek_status lsek_ep_combine_chunks(lsek_ep_domain* d, int32_t* chunk_of,
+                                   const int32_t* src_to_dest_map, int32_t recv_rows,
+                                   int32_t valid_slots, int32_t chunk_tokens, int32_t chunks,
+                                   void* stream);
+/* Token-chunked combine, step 2: lsek_ep_combine_push restricted to the rows
+ * of one chunk, which then publishes combine-chunk epoch `epoch`
+ * (lsek_ep_wait what = 2 + chunk).  order / order_off are the rows sorted by
+ * chunk (stably) and the chunk offsets [chunks + 1], as lsek_moe_route gives
+ * them for the keys chunk_of with one slot per row (permuted_idx and
+ * expert_offsets); the call pushes rows order[d] for order_off[chunk] <= d <
+ * order_off[chunk + 1] that also satisfy *row_lo <= p < *row_hi when given.
+ * A source can reduce chunk c's tokens (lsek_ep_combine_reduce on that token
+ * range) once every rank has published chunk c, while later chunks are still
+ * in flight.  Rows of earlier non-publishing pushes on the same stream are
+ * ordered before the flag.  No counterpart in the reference. */
+LSEK_API lsek_status lsek_ep_combine_push_chunk(lsek_ep_domain* d, const void* expert_out,
+                                       const int32_t* dst_rank, const int32_t* dst_row,
+                                       const float* dst_w, int32_t rows, const int32_t* row_lo,
+                                       const int32_t* row_hi, const int32_t* order,
+                                       const int32_t* order_off, int32_t chunk, uint32_t epoch,
+                                       void* stream);
 /* Down-projection GEMM with the combine fused into its epilogue: for each
  * permuted row p, bf16(dst_w[p] * bf16(H[p] . W_down[e]^T)) goes to row
  * dst_row[p] of rank dst_rank[p]'s combine buffer; then publishes combine

@@ -293,7 +293,7 @@ struct PushParams {
   int world, me;
   int32_t dest_base[kMaxPeers];  // first row of this rank's rows in each destination's recv_rows
   int64_t cap_rows;
-  size_t off_rows, off_ids, off_w;
+  size_t off_rows, off_ids, off_w, off_tok;
   uint32_t* done;
   uint32_t epoch;
 };
@@ -321,6 +321,8 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_push_kernel(
       const bool ok = row < rows && dst >= 0 && dst < pp.cap_rows;
       s_row[g] = ok ? row : -1;
       s_dst[g] = dst;
+      // The token index travels with the row (the token-chunked combine cuts by it).
+      if (ok) reinterpret_cast<int32_t*>(pp.peers.base[g] + pp.off_tok)[dst] = t;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < G * k; i += kThreads) {
@@ -401,6 +403,23 @@ __global__ void ep_combine_plan_kernel(int32_t* __restrict__ dst_rank, int32_t* 
   dst_w[p] = __ldg(w + i);
 }
 
+// Token chunk of every permuted row p of the received slots:
+// chunk_of[p] = (source token of its received row) / chunk_tokens.
+__global__ void ep_combine_chunks_kernel(int32_t* __restrict__ chunk_of,
+                                         const int32_t* __restrict__ ids,
+                                         const int32_t* __restrict__ recv_tok,
+                                         const int32_t* __restrict__ s2d, int R, int k,
+                                         int32_t valid, int chunk_tokens, int chunks) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i >= static_cast<int64_t>(R) * k) return;
+  if (__ldg(ids + i) < 0) return;
+  const int32_t p = __ldg(s2d + i);
+  if (p < 0 || p >= valid) return;
+  const int32_t t = __ldg(recv_tok + i / k);
+  const int c = t < 0 ? 0 : t / chunk_tokens;
+  chunk_of[p] = c < chunks ? c : chunks - 1;
+}
+
 // The combine without a GEMM in front (expert outputs already in memory):
 // row p of y becomes bf16(dst_w[p] * y[p]) at row dst_row[p] of rank
 // dst_rank[p]'s combine buffer; the last CTA publishes the combine epoch.
@@ -409,11 +428,18 @@ __global__ void __launch_bounds__(kThreads) ep_combine_push_kernel(
     const int32_t* __restrict__ dst_rank, const int32_t* __restrict__ dst_row,
     const float* __restrict__ dst_w, int32_t rows, const int32_t* __restrict__ row_lo,
     const int32_t* __restrict__ row_hi, int publish, int64_t cap_slots, int H, int world, int me,
-    uint32_t* done, uint32_t epoch) {
+    uint32_t* done, uint32_t epoch, const int32_t* __restrict__ order,
+    const int32_t* __restrict__ order_off, int chunk, size_t flag_offset) {
   const int nvec = H / 8;
   const int32_t p0 = row_lo ? max(__ldg(row_lo), 0) : 0;
   const int32_t p1 = row_hi ? min(__ldg(row_hi), rows) : rows;
-  for (int32_t p = p0 + blockIdx.x; p < p1; p += gridDim.x) {
+  // With `order`: the rows order[d] for d in chunk `chunk`'s range of the
+  // chunk-sorted order that lie in [p0, p1); else the rows p0 .. p1-1.
+  const int32_t d0 = order ? max(__ldg(order_off + chunk), 0) : p0;
+  const int32_t d1 = order ? min(__ldg(order_off + chunk + 1), rows) : p1;
+  for (int32_t d = d0 + blockIdx.x; d < d1; d += gridDim.x) {
+    const int32_t p = order ? __ldg(order + d) : d;
+    if (p < p0 || p >= p1) continue;
     const int32_t rk = __ldg(dst_rank + p);
     const int32_t dr = __ldg(dst_row + p);
     if (rk < 0 || rk >= world || dr < 0 || dr >= cap_slots) continue;
@@ -443,7 +469,7 @@ __global__ void __launch_bounds__(kThreads) ep_combine_push_kernel(
       }
     }
   }
-  if (publish) grid_release_to_peers(peers, world, me, kCtrlCombineFlags, done, epoch);
+  if (publish) grid_release_to_peers(peers, world, me, flag_offset, done, epoch);
   else __threadfence_system();  // ordered before the publishing call that follows on the stream
 }
 
@@ -763,6 +789,7 @@ extern "C" lsek_status lsek_ep_dispatch_push(lsek_ep_domain* h, int32_t* send_id
   pp.off_rows = d.lay.recv_rows;
   pp.off_ids = d.lay.recv_ids;
   pp.off_w = d.lay.recv_w;
+  pp.off_tok = d.lay.recv_tok;
   pp.done = reinterpret_cast<uint32_t*>(d.local + kCtrlPushDone);
   pp.epoch = epoch;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -808,10 +835,14 @@ extern "C" lsek_status lsek_ep_wait(lsek_ep_domain* h, int32_t what, uint32_t ep
                                     int64_t timeout_ns, void* stream) {
   lsek_status s = domain_check(h, "ep_wait");
   if (s != LSEK_OK) return s;
-  LSEK_REQUIRE(what == 0 || what == 1, "ep_wait: what must be 0 (dispatch) or 1 (combine)");
+  LSEK_REQUIRE(what >= 0 && what < 2 + kMaxCombineChunks,
+               "ep_wait: what must be 0 (dispatch), 1 (combine) or 2 + c (combine chunk c < %d)",
+               kMaxCombineChunks);
   const EpDomain& d = h->d;
-  const uint32_t* flags =
-      reinterpret_cast<const uint32_t*>(d.local + (what == 0 ? kCtrlDispatchFlags : kCtrlCombineFlags));
+  const size_t off = what == 0   ? kCtrlDispatchFlags
+                     : what == 1 ? kCtrlCombineFlags
+                                 : kCtrlChunkFlags + 256 * static_cast<size_t>(what - 2);
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(d.local + off);
   const uint64_t limit = timeout_ns > 0 ? static_cast<uint64_t>(timeout_ns) : kWaitLimitNs;
   ep_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
       flags, d.world, epoch, limit, what == 0 ? kDevErrEpDispatchWait : kDevErrEpCombineWait);
@@ -871,6 +902,57 @@ extern "C" lsek_status lsek_ep_combine_push(lsek_ep_domain* h, const void* exper
   ep_combine_push_kernel<<<grid, kThreads, 0, st>>>(
       peer_table(d), d.lay.back, static_cast<const __nv_bfloat16*>(expert_out), dst_rank, dst_row,
       dst_w, rows, row_lo, row_hi, publish, d.lay.cap_slots, static_cast<int>(d.H), d.world, d.rank,
-      done, epoch);
+      done, epoch, nullptr, nullptr, 0, kCtrlCombineFlags);
   return check_launch("ep_combine_push");
+}
+
+extern "C" lsek_status lsek_ep_combine_chunks(lsek_ep_domain* h, int32_t* chunk_of,
+                                              const int32_t* src_to_dest_map, int32_t recv_rows,
+                                              int32_t valid_slots, int32_t chunk_tokens,
+                                              int32_t chunks, void* stream) {
+  lsek_status s = domain_check(h, "ep_combine_chunks");
+  if (s != LSEK_OK) return s;
+  const EpDomain& d = h->d;
+  LSEK_REQUIRE(chunk_tokens >= 1, "ep_combine_chunks: chunk_tokens must be >= 1");
+  LSEK_REQUIRE(chunks >= 1 && chunks <= kMaxCombineChunks,
+               "ep_combine_chunks: chunks must be in [1, %d]", kMaxCombineChunks);
+  LSEK_REQUIRE(recv_rows >= 0 && recv_rows <= d.lay.cap_rows && valid_slots >= 0,
+               "ep_combine_chunks: bad sizes");
+  const int64_t n = static_cast<int64_t>(recv_rows) * d.k;
+  if (n == 0 || valid_slots == 0) return LSEK_OK;
+  LSEK_REQUIRE(chunk_of && src_to_dest_map, "ep_combine_chunks: NULL tensor pointer");
+  ep_combine_chunks_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0,
+                             static_cast<cudaStream_t>(stream)>>>(
+      chunk_of, reinterpret_cast<const int32_t*>(d.local + d.lay.recv_ids),
+      reinterpret_cast<const int32_t*>(d.local + d.lay.recv_tok), src_to_dest_map, recv_rows,
+      static_cast<int>(d.k), valid_slots, chunk_tokens, chunks);
+  return check_launch("ep_combine_chunks");
+}
+
+extern "C" lsek_status lsek_ep_combine_push_chunk(lsek_ep_domain* h, const void* expert_out,
+                                                  const int32_t* dst_rank, const int32_t* dst_row,
+                                                  const float* dst_w, int32_t rows,
+                                                  const int32_t* row_lo, const int32_t* row_hi,
+                                                  const int32_t* order, const int32_t* order_off,
+                                                  int32_t chunk, uint32_t epoch, void* stream) {
+  lsek_status s = domain_check(h, "ep_combine_push_chunk");
+  if (s != LSEK_OK) return s;
+  const EpDomain& d = h->d;
+  LSEK_REQUIRE(rows >= 0, "ep_combine_push_chunk: bad row count");
+  LSEK_REQUIRE(chunk >= 0 && chunk < kMaxCombineChunks,
+               "ep_combine_push_chunk: chunk must be in [0, %d)", kMaxCombineChunks);
+  LSEK_REQUIRE(rows == 0 || (expert_out && dst_rank && dst_row && dst_w && order && order_off),
+               "ep_combine_push_chunk: NULL tensor pointer");
+  LSEK_REQUIRE((row_lo == nullptr) == (row_hi == nullptr),
+               "ep_combine_push_chunk: give both row bounds or none");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t* done = reinterpret_cast<uint32_t*>(d.local + kCtrlChunkDone) + chunk;
+  LSEK_CUDA_TRY(cudaMemsetAsync(done, 0, sizeof(uint32_t), st));
+  const int64_t want = 4ll * num_sms();
+  const unsigned grid = static_cast<unsigned>(rows == 0 ? 1 : (rows < want ? rows : want));
+  ep_combine_push_kernel<<<grid, kThreads, 0, st>>>(
+      peer_table(d), d.lay.back, static_cast<const __nv_bfloat16*>(expert_out), dst_rank, dst_row,
+      dst_w, rows, row_lo, row_hi, 1, d.lay.cap_slots, static_cast<int>(d.H), d.world, d.rank,
+      done, epoch, order, order_off, chunk, kCtrlChunkFlags + 256 * static_cast<size_t>(chunk));
+  return check_launch("ep_combine_push_chunk");
 }

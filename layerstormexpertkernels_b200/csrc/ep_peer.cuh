@@ -32,14 +32,20 @@ namespace lsek {
 
 constexpr int kMaxPeers = 16;
 
-constexpr size_t kCtrlBytes = 4096;
+constexpr size_t kCtrlBytes = 16384;
 constexpr size_t kCtrlDispatchFlags = 0;    // uint32 [64]
 constexpr size_t kCtrlCombineFlags = 256;   // uint32 [64]
 constexpr size_t kCtrlPushDone = 512;       // uint32, local
 constexpr size_t kCtrlGemmDone = 768;       // uint32, local
+// Token-chunked combine: chunk c's flags (uint32 [64] at kCtrlChunkFlags +
+// 256 c) and its local CTA counter (uint32 at kCtrlChunkDone + 4 c).
+constexpr int kMaxCombineChunks = 16;
+constexpr size_t kCtrlChunkFlags = 4096;
+constexpr size_t kCtrlChunkDone = kCtrlChunkFlags + 256 * kMaxCombineChunks;
+static_assert(kCtrlChunkDone + 4 * kMaxCombineChunks <= kCtrlBytes, "control block layout");
 
 struct EpLayout {
-  size_t recv_rows, recv_ids, recv_w, back, total;
+  size_t recv_rows, recv_ids, recv_w, recv_tok, back, total;
   int64_t cap_rows, cap_slots;
 };
 
@@ -52,7 +58,8 @@ inline EpLayout ep_layout(int64_t max_tokens, int64_t H, int64_t k, int64_t G) {
   l.recv_rows = kCtrlBytes;
   l.recv_ids = l.recv_rows + align256(static_cast<size_t>(l.cap_rows * H * 2));
   l.recv_w = l.recv_ids + align256(static_cast<size_t>(l.cap_rows * k * 4));
-  l.back = l.recv_w + align256(static_cast<size_t>(l.cap_rows * k * 4));
+  l.recv_tok = l.recv_w + align256(static_cast<size_t>(l.cap_rows * k * 4));
+  l.back = l.recv_tok + align256(static_cast<size_t>(l.cap_rows * 4));
   l.total = l.back + align256(static_cast<size_t>(l.cap_slots * H * 2));
   return l;
 }

@@ -520,14 +520,23 @@ torch::Tensor ep_combine_pack(torch::Tensor expert_out, torch::Tensor s2d, torch
 
 torch::Tensor ep_combine_reduce(torch::Tensor comb_rows, torch::Tensor topk_indices,
                                 torch::Tensor pair_row, torch::Tensor slot_row,
-                                int64_t num_experts, int64_t world_size) {
+                                int64_t num_experts, int64_t world_size,
+                                c10::optional<torch::Tensor> out_opt) {
   TORCH_CHECK(comb_rows.is_cuda() && comb_rows.is_contiguous() &&
                   comb_rows.scalar_type() == at::kBFloat16,
               "ep_combine_reduce: comb_rows must be a contiguous bf16 CUDA tensor");
   check_i32_cuda(topk_indices, "ep_combine_reduce: topk_indices");
   const c10::cuda::OptionalCUDAGuard guard(comb_rows.device());
   const int64_t T = topk_indices.size(0), k = topk_indices.size(1), H = comb_rows.size(1);
-  auto out = torch::empty({T, H}, comb_rows.options());
+  torch::Tensor out;
+  if (out_opt.has_value()) {
+    out = *out_opt;
+    TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.scalar_type() == at::kBFloat16 &&
+                    out.dim() == 2 && out.size(0) == T && out.size(1) == H,
+                "ep_combine_reduce: out must be a contiguous bf16 CUDA tensor [T, H]");
+  } else {
+    out = torch::empty({T, H}, comb_rows.options());
+  }
   check_status(lsek_ep_combine_reduce(out.data_ptr(), comb_rows.data_ptr(),
                                       to_i32(comb_rows.size(0), "comb_rows"),
                                       topk_indices.data_ptr<int32_t>(), pair_row.data_ptr<int32_t>(),
@@ -679,6 +688,53 @@ void ep_combine_push(int64_t h, torch::Tensor expert_out, torch::Tensor dst_rank
                                     stream_of(expert_out)));
 }
 
+torch::Tensor ep_combine_chunks(int64_t h, torch::Tensor s2d, int64_t recv_rows,
+                                int64_t valid_slots, int64_t chunk_tokens, int64_t chunks) {
+  check_i32_cuda(s2d, "ep_combine_chunks: s2d");
+  const c10::cuda::OptionalCUDAGuard guard(s2d.device());
+  auto chunk_of = torch::empty({valid_slots}, s2d.options());
+  check_status(lsek_ep_combine_chunks(domain_of(h), chunk_of.data_ptr<int32_t>(),
+                                      s2d.data_ptr<int32_t>(), to_i32(recv_rows, "recv_rows"),
+                                      to_i32(valid_slots, "valid_slots"),
+                                      to_i32(chunk_tokens, "chunk_tokens"), to_i32(chunks, "chunks"),
+                                      stream_of(s2d)));
+  return chunk_of;
+}
+
+void ep_combine_push_chunk(int64_t h, torch::Tensor expert_out, torch::Tensor dst_rank,
+                           torch::Tensor dst_row, torch::Tensor dst_w, torch::Tensor order,
+                           torch::Tensor order_off, int64_t chunk, int64_t epoch,
+                           c10::optional<torch::Tensor> row_lo,
+                           c10::optional<torch::Tensor> row_hi) {
+  TORCH_CHECK(expert_out.is_cuda() && expert_out.is_contiguous() &&
+                  expert_out.scalar_type() == at::kBFloat16,
+              "ep_combine_push_chunk: expert_out must be a contiguous bf16 CUDA tensor");
+  check_i32_cuda(dst_rank, "ep_combine_push_chunk: dst_rank");
+  check_i32_cuda(dst_row, "ep_combine_push_chunk: dst_row");
+  check_i32_cuda(order, "ep_combine_push_chunk: order");
+  check_i32_cuda(order_off, "ep_combine_push_chunk: order_off");
+  const c10::cuda::OptionalCUDAGuard guard(expert_out.device());
+  TORCH_CHECK(dst_rank.numel() <= expert_out.size(0) && order.numel() >= dst_rank.numel() &&
+                  order_off.numel() > chunk + 1,
+              "ep_combine_push_chunk: plan rows, chunk order and outputs disagree");
+  TORCH_CHECK(row_lo.has_value() == row_hi.has_value(),
+              "ep_combine_push_chunk: give both row bounds or none");
+  const int32_t* lo = nullptr;
+  const int32_t* hi = nullptr;
+  if (row_lo.has_value()) {
+    check_i32_cuda(*row_lo, "ep_combine_push_chunk: row_lo");
+    check_i32_cuda(*row_hi, "ep_combine_push_chunk: row_hi");
+    lo = row_lo->data_ptr<int32_t>();
+    hi = row_hi->data_ptr<int32_t>();
+  }
+  check_status(lsek_ep_combine_push_chunk(
+      domain_of(h), expert_out.data_ptr(), dst_rank.data_ptr<int32_t>(),
+      dst_row.data_ptr<int32_t>(), dst_w.data_ptr<float>(), to_i32(dst_rank.numel(), "rows"), lo,
+      hi, order.data_ptr<int32_t>(), order_off.data_ptr<int32_t>(), to_i32(chunk, "chunk"),
+      static_cast<uint32_t>(epoch),
+      stream_of(expert_out)));
+}
+
 void ep_down_gemm_combine(int64_t h, torch::Tensor hact, torch::Tensor w_down,
                           torch::Tensor expert_offsets, torch::Tensor dst_rank,
                           torch::Tensor dst_row, torch::Tensor dst_w, int64_t epoch) {
@@ -799,7 +855,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_combine_pack", &ep_combine_pack, py::arg("expert_out"), py::arg("s2d"), py::arg("ids"),
         py::arg("weights"), py::arg("slot_row"), py::arg("comb_rows"));
   m.def("ep_combine_reduce", &ep_combine_reduce, py::arg("comb_rows"), py::arg("topk_indices"),
-        py::arg("pair_row"), py::arg("slot_row"), py::arg("num_experts"), py::arg("world_size"));
+        py::arg("pair_row"), py::arg("slot_row"), py::arg("num_experts"), py::arg("world_size"),
+        py::arg("out") = py::none());
+  m.def("ep_combine_chunks", &ep_combine_chunks, py::arg("domain"), py::arg("s2d"),
+        py::arg("recv_rows"), py::arg("valid_slots"), py::arg("chunk_tokens"), py::arg("chunks"));
+  m.def("ep_combine_push_chunk", &ep_combine_push_chunk, py::arg("domain"), py::arg("expert_out"),
+        py::arg("dst_rank"), py::arg("dst_row"), py::arg("dst_w"), py::arg("order"),
+        py::arg("order_off"), py::arg("chunk"), py::arg("epoch"), py::arg("row_lo") = py::none(),
+        py::arg("row_hi") = py::none());
   m.def("ep_domain_create", &ep_domain_create, py::arg("rank"), py::arg("world_size"),
         py::arg("max_tokens"), py::arg("hidden_dim"), py::arg("topk"));
   m.def("ep_domain_export", &ep_domain_export, py::arg("domain"));

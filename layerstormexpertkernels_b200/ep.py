@@ -154,14 +154,22 @@ class PeerDomain:
     Every rank allocates one buffer (liblsek lsek_ep_domain_create), the
     ranks swap its CUDA IPC handle over the process group once, and the
     dispatch / combine kernels then store straight into the owner's buffer.
-    `max_tokens` bounds the tokens of one rank per layer call.  close() (or
-    leaving a `with` block) frees the buffers after a barrier, so no peer
-    still writes into them."""
+    `max_tokens` bounds the tokens of one rank per layer call.  The combine
+    runs in `combine_chunks` token chunks of ceil(max_tokens / combine_chunks)
+    tokens (the same on every rank): a rank reduces chunk c's tokens as soon
+    as every rank has pushed its rows for them, while later chunks are still
+    in flight.  close() (or leaving a `with` block) frees the buffers after a
+    barrier, so no peer still writes into them."""
 
-    def __init__(self, max_tokens: int, hidden_dim: int, topk: int, group=None):
+    def __init__(self, max_tokens: int, hidden_dim: int, topk: int, group=None,
+                 combine_chunks: int = 4):
         ex = ProcessGroupExchange(group)
         self.group, self.world_size, self.rank = group, ex.world_size, ex.rank
         self.max_tokens, self.hidden_dim, self.topk = max_tokens, hidden_dim, topk
+        self.combine_chunks = max(1, min(int(combine_chunks), 16, max(max_tokens, 1)))
+        self.chunk_tokens = -(-max(max_tokens, 1) // self.combine_chunks)
+        self._reduce_stream = None
+        self._push_stream = None
         self.handle = _C.ep_domain_create(self.rank, self.world_size, max_tokens, hidden_dim, topk)
         try:
             if self.world_size > 1:
@@ -182,6 +190,20 @@ class PeerDomain:
          self.back) = _C.ep_domain_buffers(self.handle, hidden_dim, topk)
         self.epoch = 0
         self.mirror = HostMirror()
+
+    def reduce_stream(self) -> torch.cuda.Stream:
+        if self._reduce_stream is None:
+            self._reduce_stream = torch.cuda.Stream(device=torch.cuda.current_device())
+        return self._reduce_stream
+
+    def push_stream(self) -> torch.cuda.Stream:
+        """A high-priority stream for combine pushes: the reduces that overlap
+        them (on reduce_stream) then fill the SMs only behind the pushes'
+        CTAs, which keep the NVLink stores in flight."""
+        if self._push_stream is None:
+            self._push_stream = torch.cuda.Stream(device=torch.cuda.current_device(),
+                                                  priority=-1)
+        return self._push_stream
 
     def next_epoch(self) -> int:
         self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
@@ -304,15 +326,80 @@ def peer_combine_finish(pd: PeerDispatch, steps=DeviceSteps,
     return out
 
 
+def combine_chunk_order(pd: PeerDispatch, s2d: torch.Tensor):
+    """Rows of the combine sorted by token chunk: (order, order_off) with
+    order_off [chunks + 1] the chunk boundaries in order.  The chunk of each
+    row comes from lsek_ep_combine_chunks; the stable sort is lsek_moe_route
+    with the chunks as bins and one slot per row, so chunk c's push walks only
+    its own rows."""
+    dom = pd.domain
+    chunk_of = _C.ep_combine_chunks(dom.handle, s2d, pd.recv_rows.shape[0], pd.valid_slots,
+                                    dom.chunk_tokens, dom.combine_chunks)
+    order_off, _, order = _C.moe_route(chunk_of.view(-1, 1), dom.combine_chunks)
+    return order, order_off
+
+
+def peer_combine_chunked(pd: PeerDispatch, push_chunk: Callable[[int], None],
+                         push_stream: torch.cuda.Stream, steps=DeviceSteps,
+                         mark: Optional[Callable[[str], None]] = None) -> torch.Tensor:
+    """The combine in token chunks: push_chunk(c) enqueues, on push_stream,
+    the push of every row whose source token lies in chunk c and publishes
+    chunk c (lsek_ep_combine_push_chunk).  On the domain's reduce stream,
+    chunk c's reduce waits for that push (a stream event: the reduce never
+    spins on a kernel of its own GPU) and, bounded, for every other rank's
+    chunk-c flag, then sums its tokens' slots in fixed order; it overlaps the
+    pushes of the later chunks.  Returns the [T, H] bf16 output (bit-identical
+    to the unchunked combine: the same per-token sums)."""
+    dom = pd.domain
+    C, ct = dom.combine_chunks, dom.chunk_tokens
+    T = pd.topk_indices.shape[0]
+    G = dom.world_size
+    main = torch.cuda.current_stream()
+    red = dom.reduce_stream()
+    send_slot_row = steps.slot_scan(pd.send_ids)
+    out = torch.empty(T, dom.hidden_dim, dtype=torch.bfloat16, device=pd.topk_indices.device)
+    back = dom.back[:pd.back_rows]
+    pair_row = pd.pair_row.view(max(T, 1), G) if T > 0 else pd.pair_row.view(0, G)
+    ready = torch.cuda.Event()
+    ready.record(main)
+    push_stream.wait_event(ready)
+    for c in range(C):
+        push_chunk(c)
+        pushed = torch.cuda.Event()
+        pushed.record(push_stream)
+        red.wait_event(pushed)
+        t0, t1 = min(c * ct, T), min((c + 1) * ct, T)
+        with torch.cuda.stream(red):
+            _C.ep_wait(dom.handle, 2 + c, pd.epoch)
+            if t1 > t0:
+                steps.combine_reduce(back, pd.topk_indices[t0:t1], pair_row[t0:t1], send_slot_row,
+                                     pd.num_experts, G, out=out[t0:t1])
+    if mark:
+        main.wait_stream(push_stream)
+        mark("ep_combine_push")
+    main.wait_stream(red)
+    if mark:
+        mark("ep_combine_reduce")
+    return out
+
+
 def peer_combine(pd: PeerDispatch, expert_out: torch.Tensor, src_to_dest_map: torch.Tensor,
                  steps=DeviceSteps, mark: Optional[Callable[[str], None]] = None) -> torch.Tensor:
     """The weighted combine of expert outputs already in memory
-    ([valid_slots, H] in the order of src_to_dest_map)."""
+    ([valid_slots, H] in the order of src_to_dest_map), pushed and reduced
+    in token chunks (peer_combine_chunked)."""
     dst_rank, dst_row, dst_w = peer_combine_plan(pd, src_to_dest_map, steps)
-    _C.ep_combine_push(pd.domain.handle, expert_out, dst_rank, dst_row, dst_w, pd.epoch)
-    if mark:
-        mark("ep_combine_push")
-    return peer_combine_finish(pd, steps, mark)
+    dom = pd.domain
+    order, order_off = combine_chunk_order(pd, src_to_dest_map)
+
+    push = dom.push_stream()
+
+    def push_chunk(c):
+        with torch.cuda.stream(push):
+            _C.ep_combine_push_chunk(dom.handle, expert_out, dst_rank, dst_row, dst_w, order,
+                                     order_off, c, pd.epoch)
+
+    return peer_combine_chunked(pd, push_chunk, push, steps, mark)
 
 
 def dispatch(hidden: torch.Tensor, topk_indices: torch.Tensor, topk_weights: torch.Tensor,
@@ -424,7 +511,6 @@ class EPMoELayer:
         # "push" computes the down projection in `push_chunks` groups of
         # experts and streams each group's rows while the next one computes.
         self.push_chunks = max(1, min(push_chunks, self.local_experts))
-        self._comm_stream = None
 
     def gate(self, logits: torch.Tensor):
         return self.steps.topk_gating(logits, self.bias, self.topk, self.n_group, self.topk_group,
@@ -480,25 +566,35 @@ class EPMoELayer:
         dst_rank, dst_row, dst_w = peer_combine_plan(pd, s2d, self.steps)
         y = torch.empty(h.shape[0], self.w_down.shape[1], dtype=h.dtype, device=h.device)
         main = torch.cuda.current_stream()
-        if self._comm_stream is None:
-            self._comm_stream = torch.cuda.Stream(device=h.device)
-        comm = self._comm_stream
+        comm = pd.domain.push_stream()
         El, C = self.local_experts, self.push_chunks
         bounds = [(c * El) // C for c in range(C + 1)]
-        for c in range(C):
+        dom = pd.domain
+        order, order_off = combine_chunk_order(pd, s2d)
+        for c in range(C - 1):
             lo, hi = bounds[c], bounds[c + 1]
             _C.grouped_gemm_bf16_out(y, h, self.w_down[lo:hi], offsets[lo:hi + 1])
             ready = torch.cuda.Event()
             ready.record(main)
             comm.wait_event(ready)
             with torch.cuda.stream(comm):
-                _C.ep_combine_push(pd.domain.handle, y, dst_rank, dst_row, dst_w, pd.epoch,
+                _C.ep_combine_push(dom.handle, y, dst_rank, dst_row, dst_w, pd.epoch,
                                    row_lo=offsets[lo:lo + 1], row_hi=offsets[hi:hi + 1],
-                                   publish=c == C - 1)
-        main.wait_stream(comm)
+                                   publish=False)
+        # The last group's rows go in token chunks, each publishing its chunk
+        # (the earlier groups' rows precede them on the same stream).
+        lo, hi = bounds[C - 1], bounds[C]
+        _C.grouped_gemm_bf16_out(y, h, self.w_down[lo:hi], offsets[lo:hi + 1])
         if mark:
             mark("down_gemm_push")
-        return peer_combine_finish(pd, self.steps, mark)
+
+        def push_chunk(c):
+            with torch.cuda.stream(comm):
+                _C.ep_combine_push_chunk(dom.handle, y, dst_rank, dst_row, dst_w, order, order_off,
+                                         c, pd.epoch, row_lo=offsets[lo:lo + 1],
+                                         row_hi=offsets[hi:hi + 1])
+
+        return peer_combine_chunked(pd, push_chunk, comm, self.steps, mark)
 
     __call__ = forward
 

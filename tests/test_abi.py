@@ -202,10 +202,16 @@ def test_ep_domain_entry_points_reject_bad_arguments(lib):
     assert out.value is None
     assert lib.lsek_ep_domain_export(None, ctypes.c_void_p(16), ctypes.c_size_t(64)) == LSEK_ERR_INVALID_ARG
     assert lib.lsek_ep_wait(None, 0, 1, 0, None) == LSEK_ERR_INVALID_ARG
+    d = ctypes.c_void_p(16)
+    assert lib.lsek_ep_combine_chunks(None, d, d, 4, 4, 16, 4, None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_ep_combine_push_chunk(None, d, d, d, d, 4, None, None, d, d, 0, 1,
+                                          None) == LSEK_ERR_INVALID_ARG
     lib.lsek_ep_domain_bytes.restype = ctypes.c_size_t
     one = lib.lsek_ep_domain_bytes(8192, 7168, 8, 8)
-    # control block + recv rows [T*G, H] + ids / weights [T*G, k] + combine rows [T*k, H]
-    assert one >= 4096 + 8192 * 8 * 7168 * 2 + 2 * 8192 * 8 * 8 * 4 + 8192 * 8 * 7168 * 2
+    # control block + recv rows [T*G, H] + ids / weights [T*G, k] + source tokens [T*G]
+    # + combine rows [T*k, H]
+    assert one >= (16384 + 8192 * 8 * 7168 * 2 + 2 * 8192 * 8 * 8 * 4 + 8192 * 8 * 4
+                   + 8192 * 8 * 7168 * 2)
     assert lib.lsek_ep_domain_bytes(-1, 7168, 8, 8) == 0
     lib.lsek_ep_domain_destroy(None)  # a no-op
 
