@@ -776,10 +776,16 @@ def run_ep(args):
 
     plan = 1 + route_launches(T * world) + 1
     permute = route_launches(recv_rows * TOPK) + 1
-    if peer:  # gating, plan, counts read, push, wait, permute, gate/up, scan, combine plan,
-        # down+combine (fused) or push_chunks x (down GEMM, combine push), wait, scan, reduce
-        down = 2 * layer.push_chunks if layer.combine == "push" else 1
-        launches = 1 + plan + 1 + 1 + 1 + permute + 1 + 1 + 1 + down + 1 + 1 + 1
+    if peer and layer.combine == "push":
+        # gating, plan, counts read, dispatch push, wait, permute, gate/up, scan, combine
+        # plan, push_chunks - 1 x (down GEMM, combine push), last down GEMM, then per token
+        # chunk a push and a wait (and a reduce when the chunk holds tokens), send-side scan
+        C, ct = domain.combine_chunks, domain.chunk_tokens
+        reduces = min(C, -(-T // ct))
+        launches = (1 + plan + 1 + 1 + 1 + permute + 1 + 1 + 1 + 2 * (layer.push_chunks - 1)
+                    + 1 + 2 * C + reduces + 1)
+    elif peer:  # ... as above up to the combine plan, down+combine, wait, scan, reduce
+        launches = 1 + plan + 1 + 1 + 1 + permute + 1 + 1 + 1 + 1 + 1 + 1 + 1
     else:     # gating, plan, pack, permute, gate/up, down, scan, combine pack, scan, reduce
         launches = 1 + plan + 1 + permute + 2 + 2 + 1 + 1
     if rank == 0:

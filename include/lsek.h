@@ -417,23 +417,25 @@ LSEK_API lsek_status lsek_ep_combine_push(lsek_ep_domain* d, const void* expert_
                                  const float* dst_w, int32_t rows, const int32_t* row_lo,
                                  const int32_t* row_hi, int32_t publish, uint32_t epoch,
                                  void* stream);
-/* Token-chunked combine, step 1: chunk_of[p] = (source token of permuted
- * row p's received row) / chunk_tokens, capped at chunks - 1, for every
- * valid received slot (the same p as lsek_ep_combine_plan's).  Every rank
- * must use the same chunk_tokens and chunks (e.g. from the domain's
+/* Token-chunked combine, step 1: lsek_ep_combine_plan that also lists the
+ * rows of every token chunk.  Chunk c holds the permuted rows p whose source
+ * token t (the token's index on the rank that sent it) has
+ * t / chunk_tokens == c (capped at chunks - 1).  List c is
+ * order[c * valid_slots ...], order_count[c] entries long, in no particular
+ * order; order has chunks * valid_slots entries, order_count chunks.  Every
+ * rank must use the same chunk_tokens and chunks (e.g. from the domain's
  * max_tokens), so chunk c of every source covers the same token range.
  * chunks in [1, 16].  No counterpart in the reference. */
-LSEK_API lsek_status lsek_ep_combine_chunks(lsek_ep_domain* d, int32_t* chunk_of,
-                                   const int32_t* src_to_dest_map, int32_t recv_rows,
-                                   int32_t valid_slots, int32_t chunk_tokens, int32_t chunks,
-                                   void* stream);
+LSEK_API lsek_status lsek_ep_combine_plan_chunks(lsek_ep_domain* d, int32_t* dst_rank,
+                                        int32_t* dst_row, float* dst_w, int32_t* order,
+                                        int32_t* order_count, const int32_t* src_to_dest_map,
+                                        const int32_t* slot_row, const int32_t* counts,
+                                        int32_t recv_rows, int32_t valid_slots,
+                                        int32_t chunk_tokens, int32_t chunks, void* stream);
 /* Token-chunked combine, step 2: lsek_ep_combine_push restricted to the rows
- * of one chunk, which then publishes combine-chunk epoch `epoch`
- * (lsek_ep_wait what = 2 + chunk).  order / order_off are the rows sorted by
- * chunk (stably) and the chunk offsets [chunks + 1], as lsek_moe_route gives
- * them for the keys chunk_of with one slot per row (permuted_idx and
- * expert_offsets); the call pushes rows order[d] for order_off[chunk] <= d <
- * order_off[chunk + 1] that also satisfy *row_lo <= p < *row_hi when given.
+ * of chunk `chunk`'s list from lsek_ep_combine_plan_chunks (rows =
+ * valid_slots there; with *row_lo <= p < *row_hi also when given), which
+ * then publishes combine-chunk epoch `epoch` (lsek_ep_wait what = 2 + chunk).
  * A source can reduce chunk c's tokens (lsek_ep_combine_reduce on that token
  * range) once every rank has published chunk c, while later chunks are still
  * in flight.  Rows of earlier non-publishing pushes on the same stream are
@@ -442,7 +444,7 @@ LSEK_API lsek_status lsek_ep_combine_push_chunk(lsek_ep_domain* d, const void* e
                                        const int32_t* dst_rank, const int32_t* dst_row,
                                        const float* dst_w, int32_t rows, const int32_t* row_lo,
                                        const int32_t* row_hi, const int32_t* order,
-                                       const int32_t* order_off, int32_t chunk, uint32_t epoch,
+                                       const int32_t* order_count, int32_t chunk, uint32_t epoch,
                                        void* stream);
 /* Down-projection GEMM with the combine fused into its epilogue: for each
  * permuted row p, bf16(dst_w[p] * bf16(H[p] . W_down[e]^T)) goes to row

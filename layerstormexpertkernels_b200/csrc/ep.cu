@@ -114,20 +114,43 @@ __global__ void __launch_bounds__(kThreads) ep_dispatch_pack_kernel(
 
 // Exclusive scan of the number of valid ids (>= 0) per row:
 // slot_row[r] = valid slots in rows < r, slot_row[R] = total.  One CTA of
-// 1024 threads walks the rows in chunks.
+// 1024 threads; in each pass a thread owns up to kScanRows consecutive rows
+// and has all their loads in flight before the block-wide scan of the
+// per-thread totals (16384 rows a pass, the running total carried across
+// passes).  `vec` says ids rows are 8 int32 on a 16-byte boundary (k = 8),
+// read as two 16-byte loads.
+constexpr int kScanRows = 16;
+
+__device__ __forceinline__ int valid_ids_in_row(const int32_t* __restrict__ ids, int64_t r, int k,
+                                                bool vec) {
+  if (vec) {
+    const int4 a = __ldg(reinterpret_cast<const int4*>(ids + r * 8));
+    const int4 b = __ldg(reinterpret_cast<const int4*>(ids + r * 8) + 1);
+    return (a.x >= 0) + (a.y >= 0) + (a.z >= 0) + (a.w >= 0) + (b.x >= 0) + (b.y >= 0) +
+           (b.z >= 0) + (b.w >= 0);
+  }
+  int c = 0;
+  for (int j = 0; j < k; ++j) c += __ldg(ids + r * k + j) >= 0;
+  return c;
+}
+
 __global__ void __launch_bounds__(1024) ep_slot_scan_kernel(const int32_t* __restrict__ ids, int R,
-                                                            int k, int32_t* __restrict__ slot_row) {
+                                                            int k, int vec,
+                                                            int32_t* __restrict__ slot_row) {
   __shared__ int s_warp[33];
-  __shared__ int s_carry;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) s_carry = 0;
-  __syncthreads();
-  for (int base = 0; base < R; base += 1024) {
-    const int r = base + threadIdx.x;
-    int c = 0;
-    if (r < R)
-      for (int j = 0; j < k; ++j) c += __ldg(ids + static_cast<int64_t>(r) * k + j) >= 0;
-    int incl = c;
+  int carry = 0;
+  for (int base = 0; base < R; base += 1024 * kScanRows) {
+    const int per = min(kScanRows, (R - base + 1023) / 1024);
+    const int r0 = base + threadIdx.x * per;
+    int cnt[kScanRows];
+    int tot = 0;
+#pragma unroll
+    for (int i = 0; i < kScanRows; ++i) {
+      cnt[i] = (i < per && r0 + i < R) ? valid_ids_in_row(ids, r0 + i, k, vec != 0) : 0;
+      tot += cnt[i];
+    }
+    int incl = tot;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const int o = __shfl_up_sync(0xffffffffu, incl, off);
@@ -147,12 +170,16 @@ __global__ void __launch_bounds__(1024) ep_slot_scan_kernel(const int32_t* __res
       if (lane == 31) s_warp[32] = wi;
     }
     __syncthreads();
-    if (r < R) slot_row[r] = s_carry + s_warp[warp] + incl - c;
-    __syncthreads();
-    if (threadIdx.x == 0) s_carry += s_warp[32];
+    int run = carry + s_warp[warp] + incl - tot;
+#pragma unroll
+    for (int i = 0; i < kScanRows; ++i) {
+      if (i < per && r0 + i < R) slot_row[r0 + i] = run;
+      run += cnt[i];
+    }
+    carry += s_warp[32];
     __syncthreads();
   }
-  if (threadIdx.x == 0) slot_row[R] = s_carry;
+  if (threadIdx.x == 0) slot_row[R] = carry;
 }
 
 // One CTA per (received row, slot): the slot's weighted expert output,
@@ -381,43 +408,56 @@ struct RecvSplit {
 };
 
 // Per permuted row p (a valid received slot): the source rank, the row of
-// its back buffer that receives bf16(w * y[p]), and w.
+// its back buffer that receives bf16(w * y[p]), and w.  With kChunks, p is
+// also appended to the list of its token chunk, chunk c = (source token of
+// the received row) / chunk_tokens capped at chunks - 1: list c is
+// order[c * seg ..] and order_count[c] its length (seg = valid slots, so no
+// list can overflow).  The appends of one warp take one atomic per chunk
+// present in it; the order inside a list is arbitrary (every row has a
+// fixed destination, so the push result does not depend on it).
+template <bool kChunks>
 __global__ void ep_combine_plan_kernel(int32_t* __restrict__ dst_rank, int32_t* __restrict__ dst_row,
                                        float* __restrict__ dst_w, const int32_t* __restrict__ ids,
                                        const float* __restrict__ w, const int32_t* __restrict__ s2d,
                                        const int32_t* __restrict__ slot_row,
                                        const __grid_constant__ RecvSplit sp, int R, int k, int G,
-                                       int32_t valid) {
+                                       int32_t valid, const int32_t* __restrict__ recv_tok,
+                                       int chunk_tokens, int chunks, int32_t* __restrict__ order,
+                                       int32_t* __restrict__ order_count) {
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (i >= static_cast<int64_t>(R) * k) return;
-  if (__ldg(ids + i) < 0) return;
   const int r = static_cast<int>(i / k), j = static_cast<int>(i - static_cast<int64_t>(r) * k);
-  int src = 0;
-  while (src + 1 < G && sp.recv_start[src + 1] <= r) ++src;
-  int rank = 0;
-  for (int jj = 0; jj < j; ++jj) rank += __ldg(ids + static_cast<int64_t>(r) * k + jj) >= 0;
-  const int32_t p = __ldg(s2d + i);
-  if (p < 0 || p >= valid) return;
-  dst_rank[p] = src;
-  dst_row[p] = sp.back_base[src] + (__ldg(slot_row + r) - __ldg(slot_row + sp.recv_start[src])) + rank;
-  dst_w[p] = __ldg(w + i);
-}
-
-// Token chunk of every permuted row p of the received slots:
-// chunk_of[p] = (source token of its received row) / chunk_tokens.
-__global__ void ep_combine_chunks_kernel(int32_t* __restrict__ chunk_of,
-                                         const int32_t* __restrict__ ids,
-                                         const int32_t* __restrict__ recv_tok,
-                                         const int32_t* __restrict__ s2d, int R, int k,
-                                         int32_t valid, int chunk_tokens, int chunks) {
-  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (i >= static_cast<int64_t>(R) * k) return;
-  if (__ldg(ids + i) < 0) return;
-  const int32_t p = __ldg(s2d + i);
-  if (p < 0 || p >= valid) return;
-  const int32_t t = __ldg(recv_tok + i / k);
-  const int c = t < 0 ? 0 : t / chunk_tokens;
-  chunk_of[p] = c < chunks ? c : chunks - 1;
+  int32_t p = -1;
+  if (i < static_cast<int64_t>(R) * k && __ldg(ids + i) >= 0) {
+    p = __ldg(s2d + i);
+    if (p >= valid) p = -1;
+  }
+  if (p >= 0) {
+    int src = 0;
+    while (src + 1 < G && sp.recv_start[src + 1] <= r) ++src;
+    int rank = 0;
+    for (int jj = 0; jj < j; ++jj) rank += __ldg(ids + static_cast<int64_t>(r) * k + jj) >= 0;
+    dst_rank[p] = src;
+    dst_row[p] = sp.back_base[src] + (__ldg(slot_row + r) - __ldg(slot_row + sp.recv_start[src])) + rank;
+    dst_w[p] = __ldg(w + i);
+  }
+  if (kChunks) {
+    int c = -1;
+    if (p >= 0) {
+      const int32_t t = __ldg(recv_tok + r);
+      c = t < 0 ? 0 : min(t / chunk_tokens, chunks - 1);
+    }
+    const unsigned same = __match_any_sync(0xffffffffu, c);
+    if (c >= 0) {
+      const int lane = threadIdx.x & 31;
+      const int leader = __ffs(same) - 1;
+      int32_t at = 0;
+      if (lane == leader) at = atomicAdd(order_count + c, __popc(same));
+      at = __shfl_sync(same, at, leader);
+      unsigned below;
+      asm("mov.u32 %0, %%lanemask_lt;" : "=r"(below));
+      order[static_cast<int64_t>(c) * valid + at + __popc(same & below)] = p;
+    }
+  }
 }
 
 // The combine without a GEMM in front (expert outputs already in memory):
@@ -429,14 +469,16 @@ __global__ void __launch_bounds__(kThreads) ep_combine_push_kernel(
     const float* __restrict__ dst_w, int32_t rows, const int32_t* __restrict__ row_lo,
     const int32_t* __restrict__ row_hi, int publish, int64_t cap_slots, int H, int world, int me,
     uint32_t* done, uint32_t epoch, const int32_t* __restrict__ order,
-    const int32_t* __restrict__ order_off, int chunk, size_t flag_offset) {
+    const int32_t* __restrict__ order_count, int64_t order_stride, int chunk, size_t flag_offset) {
   const int nvec = H / 8;
   const int32_t p0 = row_lo ? max(__ldg(row_lo), 0) : 0;
   const int32_t p1 = row_hi ? min(__ldg(row_hi), rows) : rows;
-  // With `order`: the rows order[d] for d in chunk `chunk`'s range of the
-  // chunk-sorted order that lie in [p0, p1); else the rows p0 .. p1-1.
-  const int32_t d0 = order ? max(__ldg(order_off + chunk), 0) : p0;
-  const int32_t d1 = order ? min(__ldg(order_off + chunk + 1), rows) : p1;
+  // With `order`: the rows order[d] of chunk `chunk`'s list that lie in
+  // [p0, p1); else the rows p0 .. p1-1.
+  if (order != nullptr) order += chunk * order_stride;
+  const int32_t d0 = order ? 0 : p0;
+  const int64_t listed = order ? static_cast<int64_t>(__ldg(order_count + chunk)) : 0;
+  const int32_t d1 = order ? static_cast<int32_t>(listed < order_stride ? listed : order_stride) : p1;
   for (int32_t d = d0 + blockIdx.x; d < d1; d += gridDim.x) {
     const int32_t p = order ? __ldg(order + d) : d;
     if (p < p0 || p >= p1) continue;
@@ -556,7 +598,9 @@ extern "C" lsek_status lsek_ep_slot_scan(int32_t* slot_row, const int32_t* ids, 
                                          int32_t topk, void* stream) {
   LSEK_REQUIRE(rows >= 0 && topk >= 1 && topk <= 32, "ep_slot_scan: bad sizes");
   LSEK_REQUIRE(slot_row != nullptr && (rows == 0 || ids != nullptr), "ep_slot_scan: NULL pointer");
-  ep_slot_scan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(ids, rows, topk, slot_row);
+  const int vec = topk == 8 && reinterpret_cast<uintptr_t>(ids) % 16 == 0;
+  ep_slot_scan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(ids, rows, topk, vec,
+                                                                         slot_row);
   return check_launch("ep_slot_scan");
 }
 
@@ -849,22 +893,32 @@ extern "C" lsek_status lsek_ep_wait(lsek_ep_domain* h, int32_t what, uint32_t ep
   return check_launch("ep_wait");
 }
 
-extern "C" lsek_status lsek_ep_combine_plan(lsek_ep_domain* h, int32_t* dst_rank, int32_t* dst_row,
-                                            float* dst_w, const int32_t* src_to_dest_map,
-                                            const int32_t* slot_row, const int32_t* counts,
-                                            int32_t recv_rows, int32_t valid_slots, void* stream) {
-  lsek_status s = domain_check(h, "ep_combine_plan");
+static lsek_status combine_plan(lsek_ep_domain* h, int32_t* dst_rank, int32_t* dst_row,
+                                float* dst_w, const int32_t* src_to_dest_map,
+                                const int32_t* slot_row, const int32_t* counts, int32_t recv_rows,
+                                int32_t valid_slots, int32_t chunk_tokens, int32_t chunks,
+                                int32_t* order, int32_t* order_count, void* stream,
+                                const char* name) {
+  lsek_status s = domain_check(h, name);
   if (s != LSEK_OK) return s;
   const EpDomain& d = h->d;
   const int G = d.world;
-  LSEK_REQUIRE(counts != nullptr, "ep_combine_plan: counts is NULL");
+  LSEK_REQUIRE(counts != nullptr, "%s: counts is NULL", name);
   LSEK_REQUIRE(recv_rows >= 0 && recv_rows <= d.lay.cap_rows && valid_slots >= 0,
-               "ep_combine_plan: bad sizes");
+               "%s: bad sizes", name);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (chunks > 0) {
+    LSEK_REQUIRE(chunk_tokens >= 1, "%s: chunk_tokens must be >= 1", name);
+    LSEK_REQUIRE(chunks <= kMaxCombineChunks, "%s: chunks must be in [1, %d]", name,
+                 kMaxCombineChunks);
+    LSEK_REQUIRE(order_count != nullptr, "%s: order_count is NULL", name);
+    LSEK_CUDA_TRY(cudaMemsetAsync(order_count, 0, sizeof(int32_t) * chunks, st));
+  }
   RecvSplit sp;
   for (int g = 0; g <= kMaxPeers; ++g) sp.recv_start[g] = 0;
   for (int g = 0; g < kMaxPeers; ++g) sp.back_base[g] = 0;
   for (int src = 0; src <= G; ++src) sp.recv_start[src] = static_cast<int32_t>(col_sum(counts, G, src, d.rank, 0));
-  LSEK_REQUIRE(sp.recv_start[G] == recv_rows, "ep_combine_plan: recv_rows disagrees with counts");
+  LSEK_REQUIRE(sp.recv_start[G] == recv_rows, "%s: recv_rows disagrees with counts", name);
   for (int src = 0; src < G; ++src) {
     int64_t b = 0;
     for (int g = 0; g < d.rank; ++g) b += counts[(static_cast<int64_t>(src) * G + g) * 2 + 1];
@@ -873,13 +927,38 @@ extern "C" lsek_status lsek_ep_combine_plan(lsek_ep_domain* h, int32_t* dst_rank
   const int64_t n = static_cast<int64_t>(recv_rows) * d.k;
   if (n == 0 || valid_slots == 0) return LSEK_OK;
   LSEK_REQUIRE(dst_rank && dst_row && dst_w && src_to_dest_map && slot_row,
-               "ep_combine_plan: NULL tensor pointer");
-  ep_combine_plan_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0,
-                           static_cast<cudaStream_t>(stream)>>>(
+               "%s: NULL tensor pointer", name);
+  LSEK_REQUIRE(chunks == 0 || order != nullptr, "%s: order is NULL", name);
+  auto kernel = chunks > 0 ? ep_combine_plan_kernel<true> : ep_combine_plan_kernel<false>;
+  kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, st>>>(
       dst_rank, dst_row, dst_w, reinterpret_cast<const int32_t*>(d.local + d.lay.recv_ids),
       reinterpret_cast<const float*>(d.local + d.lay.recv_w), src_to_dest_map, slot_row, sp,
-      recv_rows, static_cast<int>(d.k), G, valid_slots);
-  return check_launch("ep_combine_plan");
+      recv_rows, static_cast<int>(d.k), G, valid_slots,
+      reinterpret_cast<const int32_t*>(d.local + d.lay.recv_tok), chunk_tokens, chunks, order,
+      order_count);
+  return check_launch(name);
+}
+
+extern "C" lsek_status lsek_ep_combine_plan(lsek_ep_domain* h, int32_t* dst_rank, int32_t* dst_row,
+                                            float* dst_w, const int32_t* src_to_dest_map,
+                                            const int32_t* slot_row, const int32_t* counts,
+                                            int32_t recv_rows, int32_t valid_slots, void* stream) {
+  return combine_plan(h, dst_rank, dst_row, dst_w, src_to_dest_map, slot_row, counts, recv_rows,
+                      valid_slots, 0, 0, nullptr, nullptr, stream, "ep_combine_plan");
+}
+
+extern "C" lsek_status lsek_ep_combine_plan_chunks(lsek_ep_domain* h, int32_t* dst_rank,
+                                                   int32_t* dst_row, float* dst_w, int32_t* order,
+                                                   int32_t* order_count,
+                                                   const int32_t* src_to_dest_map,
+                                                   const int32_t* slot_row, const int32_t* counts,
+                                                   int32_t recv_rows, int32_t valid_slots,
+                                                   int32_t chunk_tokens, int32_t chunks,
+                                                   void* stream) {
+  if (chunks < 1) return fail(LSEK_ERR_INVALID_ARG, "ep_combine_plan_chunks: chunks must be >= 1");
+  return combine_plan(h, dst_rank, dst_row, dst_w, src_to_dest_map, slot_row, counts, recv_rows,
+                      valid_slots, chunk_tokens, chunks, order, order_count, stream,
+                      "ep_combine_plan_chunks");
 }
 
 extern "C" lsek_status lsek_ep_combine_push(lsek_ep_domain* h, const void* expert_out,
@@ -902,38 +981,15 @@ extern "C" lsek_status lsek_ep_combine_push(lsek_ep_domain* h, const void* exper
   ep_combine_push_kernel<<<grid, kThreads, 0, st>>>(
       peer_table(d), d.lay.back, static_cast<const __nv_bfloat16*>(expert_out), dst_rank, dst_row,
       dst_w, rows, row_lo, row_hi, publish, d.lay.cap_slots, static_cast<int>(d.H), d.world, d.rank,
-      done, epoch, nullptr, nullptr, 0, kCtrlCombineFlags);
+      done, epoch, nullptr, nullptr, 0, 0, kCtrlCombineFlags);
   return check_launch("ep_combine_push");
-}
-
-extern "C" lsek_status lsek_ep_combine_chunks(lsek_ep_domain* h, int32_t* chunk_of,
-                                              const int32_t* src_to_dest_map, int32_t recv_rows,
-                                              int32_t valid_slots, int32_t chunk_tokens,
-                                              int32_t chunks, void* stream) {
-  lsek_status s = domain_check(h, "ep_combine_chunks");
-  if (s != LSEK_OK) return s;
-  const EpDomain& d = h->d;
-  LSEK_REQUIRE(chunk_tokens >= 1, "ep_combine_chunks: chunk_tokens must be >= 1");
-  LSEK_REQUIRE(chunks >= 1 && chunks <= kMaxCombineChunks,
-               "ep_combine_chunks: chunks must be in [1, %d]", kMaxCombineChunks);
-  LSEK_REQUIRE(recv_rows >= 0 && recv_rows <= d.lay.cap_rows && valid_slots >= 0,
-               "ep_combine_chunks: bad sizes");
-  const int64_t n = static_cast<int64_t>(recv_rows) * d.k;
-  if (n == 0 || valid_slots == 0) return LSEK_OK;
-  LSEK_REQUIRE(chunk_of && src_to_dest_map, "ep_combine_chunks: NULL tensor pointer");
-  ep_combine_chunks_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0,
-                             static_cast<cudaStream_t>(stream)>>>(
-      chunk_of, reinterpret_cast<const int32_t*>(d.local + d.lay.recv_ids),
-      reinterpret_cast<const int32_t*>(d.local + d.lay.recv_tok), src_to_dest_map, recv_rows,
-      static_cast<int>(d.k), valid_slots, chunk_tokens, chunks);
-  return check_launch("ep_combine_chunks");
 }
 
 extern "C" lsek_status lsek_ep_combine_push_chunk(lsek_ep_domain* h, const void* expert_out,
                                                   const int32_t* dst_rank, const int32_t* dst_row,
                                                   const float* dst_w, int32_t rows,
                                                   const int32_t* row_lo, const int32_t* row_hi,
-                                                  const int32_t* order, const int32_t* order_off,
+                                                  const int32_t* order, const int32_t* order_count,
                                                   int32_t chunk, uint32_t epoch, void* stream) {
   lsek_status s = domain_check(h, "ep_combine_push_chunk");
   if (s != LSEK_OK) return s;
@@ -941,7 +997,7 @@ extern "C" lsek_status lsek_ep_combine_push_chunk(lsek_ep_domain* h, const void*
   LSEK_REQUIRE(rows >= 0, "ep_combine_push_chunk: bad row count");
   LSEK_REQUIRE(chunk >= 0 && chunk < kMaxCombineChunks,
                "ep_combine_push_chunk: chunk must be in [0, %d)", kMaxCombineChunks);
-  LSEK_REQUIRE(rows == 0 || (expert_out && dst_rank && dst_row && dst_w && order && order_off),
+  LSEK_REQUIRE(rows == 0 || (expert_out && dst_rank && dst_row && dst_w && order && order_count),
                "ep_combine_push_chunk: NULL tensor pointer");
   LSEK_REQUIRE((row_lo == nullptr) == (row_hi == nullptr),
                "ep_combine_push_chunk: give both row bounds or none");
@@ -953,6 +1009,7 @@ extern "C" lsek_status lsek_ep_combine_push_chunk(lsek_ep_domain* h, const void*
   ep_combine_push_kernel<<<grid, kThreads, 0, st>>>(
       peer_table(d), d.lay.back, static_cast<const __nv_bfloat16*>(expert_out), dst_rank, dst_row,
       dst_w, rows, row_lo, row_hi, 1, d.lay.cap_slots, static_cast<int>(d.H), d.world, d.rank,
-      done, epoch, order, order_off, chunk, kCtrlChunkFlags + 256 * static_cast<size_t>(chunk));
+      done, epoch, rows == 0 ? nullptr : order, order_count, static_cast<int64_t>(rows), chunk,
+      kCtrlChunkFlags + 256 * static_cast<size_t>(chunk));
   return check_launch("ep_combine_push_chunk");
 }

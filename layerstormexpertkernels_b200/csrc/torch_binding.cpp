@@ -688,22 +688,34 @@ void ep_combine_push(int64_t h, torch::Tensor expert_out, torch::Tensor dst_rank
                                     stream_of(expert_out)));
 }
 
-torch::Tensor ep_combine_chunks(int64_t h, torch::Tensor s2d, int64_t recv_rows,
-                                int64_t valid_slots, int64_t chunk_tokens, int64_t chunks) {
-  check_i32_cuda(s2d, "ep_combine_chunks: s2d");
+// lsek_ep_combine_plan_chunks: [dst_rank, dst_row, dst_w, order [chunks *
+// valid_slots], order_count [chunks]].
+std::vector<torch::Tensor> ep_combine_plan_chunks(int64_t h, torch::Tensor s2d,
+                                                  torch::Tensor slot_row, torch::Tensor counts,
+                                                  int64_t recv_rows, int64_t valid_slots,
+                                                  int64_t chunk_tokens, int64_t chunks) {
+  check_counts(counts);
+  check_i32_cuda(s2d, "ep_combine_plan_chunks: s2d");
+  check_i32_cuda(slot_row, "ep_combine_plan_chunks: slot_row");
+  TORCH_CHECK(chunks >= 1 && chunks <= 16, "ep_combine_plan_chunks: chunks must be in [1, 16]");
   const c10::cuda::OptionalCUDAGuard guard(s2d.device());
-  auto chunk_of = torch::empty({valid_slots}, s2d.options());
-  check_status(lsek_ep_combine_chunks(domain_of(h), chunk_of.data_ptr<int32_t>(),
-                                      s2d.data_ptr<int32_t>(), to_i32(recv_rows, "recv_rows"),
-                                      to_i32(valid_slots, "valid_slots"),
-                                      to_i32(chunk_tokens, "chunk_tokens"), to_i32(chunks, "chunks"),
-                                      stream_of(s2d)));
-  return chunk_of;
+  auto dst_rank = torch::empty({valid_slots}, s2d.options());
+  auto dst_row = torch::empty({valid_slots}, s2d.options());
+  auto dst_w = torch::empty({valid_slots}, s2d.options().dtype(at::kFloat));
+  auto order = torch::empty({chunks * valid_slots}, s2d.options());
+  auto order_count = torch::empty({chunks}, s2d.options());
+  check_status(lsek_ep_combine_plan_chunks(
+      domain_of(h), dst_rank.data_ptr<int32_t>(), dst_row.data_ptr<int32_t>(),
+      dst_w.data_ptr<float>(), order.data_ptr<int32_t>(), order_count.data_ptr<int32_t>(),
+      s2d.data_ptr<int32_t>(), slot_row.data_ptr<int32_t>(), counts.data_ptr<int32_t>(),
+      to_i32(recv_rows, "recv_rows"), to_i32(valid_slots, "valid_slots"),
+      to_i32(chunk_tokens, "chunk_tokens"), to_i32(chunks, "chunks"), stream_of(s2d)));
+  return {dst_rank, dst_row, dst_w, order, order_count};
 }
 
 void ep_combine_push_chunk(int64_t h, torch::Tensor expert_out, torch::Tensor dst_rank,
                            torch::Tensor dst_row, torch::Tensor dst_w, torch::Tensor order,
-                           torch::Tensor order_off, int64_t chunk, int64_t epoch,
+                           torch::Tensor order_count, int64_t chunk, int64_t epoch,
                            c10::optional<torch::Tensor> row_lo,
                            c10::optional<torch::Tensor> row_hi) {
   TORCH_CHECK(expert_out.is_cuda() && expert_out.is_contiguous() &&
@@ -712,11 +724,12 @@ void ep_combine_push_chunk(int64_t h, torch::Tensor expert_out, torch::Tensor ds
   check_i32_cuda(dst_rank, "ep_combine_push_chunk: dst_rank");
   check_i32_cuda(dst_row, "ep_combine_push_chunk: dst_row");
   check_i32_cuda(order, "ep_combine_push_chunk: order");
-  check_i32_cuda(order_off, "ep_combine_push_chunk: order_off");
+  check_i32_cuda(order_count, "ep_combine_push_chunk: order_count");
   const c10::cuda::OptionalCUDAGuard guard(expert_out.device());
-  TORCH_CHECK(dst_rank.numel() <= expert_out.size(0) && order.numel() >= dst_rank.numel() &&
-                  order_off.numel() > chunk + 1,
-              "ep_combine_push_chunk: plan rows, chunk order and outputs disagree");
+  TORCH_CHECK(chunk >= 0 && order_count.numel() > chunk, "ep_combine_push_chunk: chunk out of range");
+  TORCH_CHECK(dst_rank.numel() <= expert_out.size(0) &&
+                  order.numel() >= (chunk + 1) * dst_rank.numel(),
+              "ep_combine_push_chunk: plan rows, chunk lists and outputs disagree");
   TORCH_CHECK(row_lo.has_value() == row_hi.has_value(),
               "ep_combine_push_chunk: give both row bounds or none");
   const int32_t* lo = nullptr;
@@ -730,7 +743,7 @@ void ep_combine_push_chunk(int64_t h, torch::Tensor expert_out, torch::Tensor ds
   check_status(lsek_ep_combine_push_chunk(
       domain_of(h), expert_out.data_ptr(), dst_rank.data_ptr<int32_t>(),
       dst_row.data_ptr<int32_t>(), dst_w.data_ptr<float>(), to_i32(dst_rank.numel(), "rows"), lo,
-      hi, order.data_ptr<int32_t>(), order_off.data_ptr<int32_t>(), to_i32(chunk, "chunk"),
+      hi, order.data_ptr<int32_t>(), order_count.data_ptr<int32_t>(), to_i32(chunk, "chunk"),
       static_cast<uint32_t>(epoch),
       stream_of(expert_out)));
 }
@@ -857,11 +870,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_combine_reduce", &ep_combine_reduce, py::arg("comb_rows"), py::arg("topk_indices"),
         py::arg("pair_row"), py::arg("slot_row"), py::arg("num_experts"), py::arg("world_size"),
         py::arg("out") = py::none());
-  m.def("ep_combine_chunks", &ep_combine_chunks, py::arg("domain"), py::arg("s2d"),
-        py::arg("recv_rows"), py::arg("valid_slots"), py::arg("chunk_tokens"), py::arg("chunks"));
+  m.def("ep_combine_plan_chunks", &ep_combine_plan_chunks, py::arg("domain"), py::arg("s2d"),
+        py::arg("slot_row"), py::arg("counts"), py::arg("recv_rows"), py::arg("valid_slots"),
+        py::arg("chunk_tokens"), py::arg("chunks"));
   m.def("ep_combine_push_chunk", &ep_combine_push_chunk, py::arg("domain"), py::arg("expert_out"),
         py::arg("dst_rank"), py::arg("dst_row"), py::arg("dst_w"), py::arg("order"),
-        py::arg("order_off"), py::arg("chunk"), py::arg("epoch"), py::arg("row_lo") = py::none(),
+        py::arg("order_count"), py::arg("chunk"), py::arg("epoch"), py::arg("row_lo") = py::none(),
         py::arg("row_hi") = py::none());
   m.def("ep_domain_create", &ep_domain_create, py::arg("rank"), py::arg("world_size"),
         py::arg("max_tokens"), py::arg("hidden_dim"), py::arg("topk"));

@@ -326,17 +326,16 @@ def peer_combine_finish(pd: PeerDispatch, steps=DeviceSteps,
     return out
 
 
-def combine_chunk_order(pd: PeerDispatch, s2d: torch.Tensor):
-    """Rows of the combine sorted by token chunk: (order, order_off) with
-    order_off [chunks + 1] the chunk boundaries in order.  The chunk of each
-    row comes from lsek_ep_combine_chunks; the stable sort is lsek_moe_route
-    with the chunks as bins and one slot per row, so chunk c's push walks only
-    its own rows."""
+def peer_combine_plan_chunked(pd: PeerDispatch, src_to_dest_map: torch.Tensor,
+                              steps=DeviceSteps):
+    """peer_combine_plan plus the rows of every token chunk, in one kernel
+    (lsek_ep_combine_plan_chunks): (dst_rank, dst_row, dst_w, order,
+    order_count), chunk c's rows being order[c * valid_slots :][:order_count[c]]."""
     dom = pd.domain
-    chunk_of = _C.ep_combine_chunks(dom.handle, s2d, pd.recv_rows.shape[0], pd.valid_slots,
-                                    dom.chunk_tokens, dom.combine_chunks)
-    order_off, _, order = _C.moe_route(chunk_of.view(-1, 1), dom.combine_chunks)
-    return order, order_off
+    slot_row = steps.slot_scan(pd.recv_ids)
+    return _C.ep_combine_plan_chunks(dom.handle, src_to_dest_map, slot_row, pd.counts,
+                                     pd.recv_rows.shape[0], pd.valid_slots, dom.chunk_tokens,
+                                     dom.combine_chunks)
 
 
 def peer_combine_chunked(pd: PeerDispatch, push_chunk: Callable[[int], None],
@@ -356,13 +355,15 @@ def peer_combine_chunked(pd: PeerDispatch, push_chunk: Callable[[int], None],
     G = dom.world_size
     main = torch.cuda.current_stream()
     red = dom.reduce_stream()
-    send_slot_row = steps.slot_scan(pd.send_ids)
     out = torch.empty(T, dom.hidden_dim, dtype=torch.bfloat16, device=pd.topk_indices.device)
     back = dom.back[:pd.back_rows]
     pair_row = pd.pair_row.view(max(T, 1), G) if T > 0 else pd.pair_row.view(0, G)
     ready = torch.cuda.Event()
     ready.record(main)
     push_stream.wait_event(ready)
+    red.wait_event(ready)
+    with torch.cuda.stream(red):  # runs beside the first push
+        send_slot_row = steps.slot_scan(pd.send_ids)
     for c in range(C):
         push_chunk(c)
         pushed = torch.cuda.Event()
@@ -388,16 +389,19 @@ def peer_combine(pd: PeerDispatch, expert_out: torch.Tensor, src_to_dest_map: to
     """The weighted combine of expert outputs already in memory
     ([valid_slots, H] in the order of src_to_dest_map), pushed and reduced
     in token chunks (peer_combine_chunked)."""
-    dst_rank, dst_row, dst_w = peer_combine_plan(pd, src_to_dest_map, steps)
     dom = pd.domain
-    order, order_off = combine_chunk_order(pd, src_to_dest_map)
-
     push = dom.push_stream()
+    start = torch.cuda.Event()
+    start.record(torch.cuda.current_stream())
+    push.wait_event(start)
+    with torch.cuda.stream(push):
+        dst_rank, dst_row, dst_w, order, count = peer_combine_plan_chunked(pd, src_to_dest_map,
+                                                                           steps)
 
     def push_chunk(c):
         with torch.cuda.stream(push):
             _C.ep_combine_push_chunk(dom.handle, expert_out, dst_rank, dst_row, dst_w, order,
-                                     order_off, c, pd.epoch)
+                                     count, c, pd.epoch)
 
     return peer_combine_chunked(pd, push_chunk, push, steps, mark)
 
@@ -562,15 +566,19 @@ class EPMoELayer:
     def _down_and_push(self, pd, h, offsets, s2d, mark):
         """Down projection in groups of experts; each group's weighted rows
         go to their source ranks on a second stream while the next group
-        computes, and the last push publishes the combine epoch."""
-        dst_rank, dst_row, dst_w = peer_combine_plan(pd, s2d, self.steps)
-        y = torch.empty(h.shape[0], self.w_down.shape[1], dtype=h.dtype, device=h.device)
+        computes, and the last group's rows go in token chunks.  The combine
+        plan runs on the push stream beside the first GEMM."""
+        dom = pd.domain
         main = torch.cuda.current_stream()
-        comm = pd.domain.push_stream()
+        comm = dom.push_stream()
+        start = torch.cuda.Event()
+        start.record(main)
+        comm.wait_event(start)
+        with torch.cuda.stream(comm):
+            dst_rank, dst_row, dst_w, order, count = peer_combine_plan_chunked(pd, s2d, self.steps)
+        y = torch.empty(h.shape[0], self.w_down.shape[1], dtype=h.dtype, device=h.device)
         El, C = self.local_experts, self.push_chunks
         bounds = [(c * El) // C for c in range(C + 1)]
-        dom = pd.domain
-        order, order_off = combine_chunk_order(pd, s2d)
         for c in range(C - 1):
             lo, hi = bounds[c], bounds[c + 1]
             _C.grouped_gemm_bf16_out(y, h, self.w_down[lo:hi], offsets[lo:hi + 1])
@@ -590,7 +598,7 @@ class EPMoELayer:
 
         def push_chunk(c):
             with torch.cuda.stream(comm):
-                _C.ep_combine_push_chunk(dom.handle, y, dst_rank, dst_row, dst_w, order, order_off,
+                _C.ep_combine_push_chunk(dom.handle, y, dst_rank, dst_row, dst_w, order, count,
                                          c, pd.epoch, row_lo=offsets[lo:lo + 1],
                                          row_hi=offsets[hi:hi + 1])
 

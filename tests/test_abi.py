@@ -203,7 +203,10 @@ def test_ep_domain_entry_points_reject_bad_arguments(lib):
     assert lib.lsek_ep_domain_export(None, ctypes.c_void_p(16), ctypes.c_size_t(64)) == LSEK_ERR_INVALID_ARG
     assert lib.lsek_ep_wait(None, 0, 1, 0, None) == LSEK_ERR_INVALID_ARG
     d = ctypes.c_void_p(16)
-    assert lib.lsek_ep_combine_chunks(None, d, d, 4, 4, 16, 4, None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_ep_combine_plan_chunks(None, d, d, d, d, d, d, d, d, 4, 4, 16, 4,
+                                           None) == LSEK_ERR_INVALID_ARG
+    assert lib.lsek_ep_combine_plan_chunks(None, d, d, d, d, d, d, d, d, 4, 4, 16, 0,
+                                           None) == LSEK_ERR_INVALID_ARG
     assert lib.lsek_ep_combine_push_chunk(None, d, d, d, d, 4, None, None, d, d, 0, 1,
                                           None) == LSEK_ERR_INVALID_ARG
     lib.lsek_ep_domain_bytes.restype = ctypes.c_size_t

@@ -250,6 +250,63 @@ def test_peer_combine_push_one_rank():
     assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
 
 
+@pytest.mark.parametrize("R,k,offset", [(1, 8, 0), (1023, 8, 0), (1025, 8, 1), (16384, 8, 0),
+                                        (16385, 8, 0), (50000, 8, 1), (20000, 5, 0), (3, 1, 0)])
+def test_slot_scan_sizes(R, k, offset):
+    """The one-CTA slot scan across its pass boundary (16384 rows a pass),
+    with 16-byte row loads (k = 8 on a 16-byte boundary) and scalar loads
+    (other k, or a view that starts 4 bytes past the boundary)."""
+    import layerstormexpertkernels_b200 as P
+    rng = np.random.default_rng(R * 7 + k)
+    ids = rng.integers(-1, 6, size=R * k + offset, dtype=np.int32)  # about 1 in 7 invalid
+    view = dev(ids)[offset:].view(R, k)
+    scan = P._C.ep_slot_scan(view)
+    sync_and_check_device_error()
+    assert np.array_equal(scan.cpu().numpy(), EO.ep_slot_scan(ids[offset:].reshape(R, k)))
+
+
+def test_combine_plan_chunks_lists_every_row_once():
+    """lsek_ep_combine_plan_chunks gives the plan of lsek_ep_combine_plan and
+    chunk lists that hold every permuted row exactly once, each in the chunk
+    of its source token (token // chunk_tokens, the last chunk taking the
+    rest)."""
+    import layerstormexpertkernels_b200 as P
+    from layerstormexpertkernels_b200 import ep as EP
+    T, E, H, k, C = 1000, 64, 64, 8, 3
+    idx, w = _routing(T, E, k, seed=9)
+    hidden = MO.bf16_round(np.random.default_rng(2).standard_normal((T, H), dtype=np.float32))
+    with EP.PeerDomain(max_tokens=1024, hidden_dim=H, topk=k, combine_chunks=C) as dom:
+        pd = EP.peer_dispatch(dom, bf16_dev(hidden), dev(idx), dev(w), E)
+        permuted, _, s2d, _ = P._C.ep_expert_permute(pd.recv_rows, pd.recv_ids, E, pd.valid_slots)
+        R, V = pd.recv_rows.shape[0], pd.valid_slots
+        slot_row = P._C.ep_slot_scan(pd.recv_ids)
+        plain = P._C.ep_combine_plan(dom.handle, s2d, slot_row, pd.counts, R, V)
+        dr, drow, dw, order, count = P._C.ep_combine_plan_chunks(
+            dom.handle, s2d, slot_row, pd.counts, R, V, dom.chunk_tokens, C)
+        EP.peer_combine(pd, permuted, s2d)  # completes the epoch
+        sync_and_check_device_error()
+        ids = pd.recv_ids.cpu().numpy()
+    assert torch.equal(dr, plain[0]) and torch.equal(drow, plain[1])
+    assert torch.equal(dw.view(torch.int32), plain[2].view(torch.int32))
+    ct = dom.chunk_tokens
+    assert ct == 342
+    _, _, _, row_pair = P._C.ep_plan(dev(idx), E, 1)
+    token = row_pair.cpu().numpy()[:R]
+    p_of = s2d.cpu().numpy().reshape(R, k)
+    want = np.full(V, -1)
+    for r in range(R):
+        for j in range(k):
+            if ids[r, j] >= 0 and 0 <= p_of[r, j] < V:
+                want[p_of[r, j]] = min(token[r] // ct, C - 1)
+    assert (want >= 0).all()
+    order, count = order.cpu().numpy().reshape(C, V), count.cpu().numpy()
+    assert count.sum() == V
+    seen = np.concatenate([order[c, :count[c]] for c in range(C)])
+    assert np.array_equal(np.sort(seen), np.arange(V))
+    for c in range(C):
+        assert (want[order[c, :count[c]]] == c).all(), c
+
+
 def test_peer_wait_expires_with_status():
     """A wait on an epoch nobody publishes gives up after its limit and
     records kDevErrEpDispatchWait (4); the context stays usable."""
