@@ -467,8 +467,9 @@ def run_ours(args):
                        "hidden": HIDDEN, "inter": INTER, "experts": E, "topk": TOPK,
                        "parallelism": "replicas" if world > 1 else "single",
                        "l2": "inputs larger than L2: 22.5 GB of expert weights per step"},
-            # gating, route (1 or 3 kernels), row copy, gate/up GEMM, down GEMM, unpermute
-            "gpu_launches": (5 + route_launches(T * TOPK)) * args.steps,
+            # gating, route (one kernel), row copy (T > 64; smaller T gathers the rows in the
+            # gate/up GEMM's loads), gate/up GEMM, down GEMM, unpermute
+            "gpu_launches": (5 + (T > 64)) * args.steps,
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": T * HIDDEN * 2 + T * E * 4,
                     "d2h_bytes_per_step": T * HIDDEN * 2,

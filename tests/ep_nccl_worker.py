@@ -5,7 +5,9 @@ fused into the down GEMM; "peer-push": peer memory with a separate combine
 kernel; "replicated": every rank holds the same tokens and the per-slot
 rows are SUM all-reduced), then the
 one-GPU canonical path on this rank's tokens with all experts, and writes
-"bit-exact" to <out_dir>/ok<rank> when every call agrees."""
+"bit-exact" to <out_dir>/ok<rank> when every call agrees.  With a third
+argument "cfg3" the shapes are BASELINE cfg3's: 8192 tokens per rank, 256
+experts, H = 7168, I = 2048, top-8."""
 from __future__ import annotations
 
 import datetime
@@ -21,7 +23,7 @@ for p in (ROOT, os.path.join(ROOT, "tests")):
         sys.path.insert(0, p)
 
 
-def main(out_dir: str, transport: str) -> int:
+def main(out_dir: str, transport: str, shape: str = "small") -> int:
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
@@ -32,8 +34,15 @@ def main(out_dir: str, transport: str) -> int:
         from test_gpu_ep import E_L, H_L, K_L, _layer_setup, canonical_gpu
         from layerstormexpertkernels_b200.ep import EPMoELayer, PeerDomain
 
-        tokens = [300 + 57 * r for r in range(world)]
-        w_gu, w_down, toks = _layer_setup(world, tokens)
+        if shape == "cfg3":
+            from layerstormexpertkernels_b200.synthetic import expert_weights, token_inputs
+            E_L, H_L, K_L = 256, 7168, 8
+            tokens = [8192] * world
+            w_gu, w_down = expert_weights(E_L, H_L, 2048, device="cuda", seed_base=9000)
+            toks = [token_inputs(t, E_L, H_L, seed=300 + r) for r, t in enumerate(tokens)]
+        else:
+            tokens = [300 + 57 * r for r in range(world)]
+            w_gu, w_down, toks = _layer_setup(world, tokens)
         El = E_L // world
         bias = toks[0].bias.cuda()
         dom = PeerDomain(max(tokens), H_L, K_L) if transport.startswith("peer") else None
@@ -43,13 +52,13 @@ def main(out_dir: str, transport: str) -> int:
                            domain=dom, combine=combine)
         if transport == "replicated":  # every rank holds rank 0's tokens
             from layerstormexpertkernels_b200.ep import replicated_forward
-            ref = canonical_gpu(toks[0], w_gu, w_down, bias)
+            ref = canonical_gpu(toks[0], w_gu, w_down, bias, E_L, K_L)
             run = lambda: replicated_forward(
                 toks[0].hidden.cuda(), toks[0].logits.cuda(), bias,
                 w_gu[rank * El:(rank + 1) * El].contiguous(),
                 w_down[rank * El:(rank + 1) * El].contiguous(), E_L, topk=K_L)
         else:
-            ref = canonical_gpu(toks[rank], w_gu, w_down, bias)
+            ref = canonical_gpu(toks[rank], w_gu, w_down, bias, E_L, K_L)
             run = lambda: layer(toks[rank].hidden.cuda(), toks[rank].logits.cuda())
         same = True
         for _ in range(3):
@@ -68,4 +77,5 @@ def main(out_dir: str, transport: str) -> int:
 
 
 if __name__ == "__main__":
-    sys.exit(main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "nccl"))
+    sys.exit(main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "nccl",
+                  sys.argv[3] if len(sys.argv) > 3 else "small"))

@@ -137,15 +137,15 @@ def _layer_setup(G, tokens):
     return w_gu, w_down, toks
 
 
-def canonical_gpu(x, w_gu, w_down, bias):
+def canonical_gpu(x, w_gu, w_down, bias, E=E_L, k=K_L):
     """The one-GPU canonical path through the reference-surface ops."""
     import layerstormexpertkernels_b200 as P
     hidden, logits = x.hidden.cuda(), x.logits.cuda()
-    w, idx = P.topk_gating(logits, bias, K_L, 8, 4, 2.5, True)
-    permuted, offs, s2d, _ = P.moe_permute(hidden, idx, E_L)
+    w, idx = P.topk_gating(logits, bias, k, 8, 4, 2.5, True)
+    permuted, offs, s2d, _ = P.moe_permute(hidden, idx, E)
     h = P.grouped_gemm_swiglu_bf16(permuted, w_gu, offs)
     y = P.grouped_gemm_bf16(h, w_down, offs)
-    perslot = P.moe_unpermute_bf16_perslot(y, w, s2d, hidden.shape[0], K_L)
+    perslot = P.moe_unpermute_bf16_perslot(y, w, s2d, hidden.shape[0], k)
     return P.moe_combine_reduce_slots_bf16_to_bf16(perslot)
 
 
@@ -334,6 +334,26 @@ def test_ep_layer_two_gpus(tmp_path, transport):
            os.path.join(ROOT, "tests", "ep_nccl_worker.py"), str(tmp_path), transport]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     res = subprocess.run(["timeout", "-k", "30", "600"] + cmd, cwd=ROOT, env=env,
+                         capture_output=True, text=True)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    for r in range(2):
+        assert (tmp_path / f"ok{r}").read_text() == "bit-exact"
+
+
+@pytest.mark.parametrize("transport", ["peer-push", "nccl"])
+def test_ep_layer_two_gpus_cfg3_shape(tmp_path, transport):
+    """The EP layer at the full cfg3 shape (T = 8192 tokens per rank, E = 256,
+    H = 7168, I = 2048, top-8 of 8 groups / 4 kept) on two processes, each
+    rank's output bit-identical to the one-GPU canonical path with all 256
+    experts on its GPU."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    port = {"peer-push": "29651", "nccl": "29653"}[transport]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", port,
+           os.path.join(ROOT, "tests", "ep_nccl_worker.py"), str(tmp_path), transport, "cfg3"]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    res = subprocess.run(["timeout", "-k", "30", "900"] + cmd, cwd=ROOT, env=env,
                          capture_output=True, text=True)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     for r in range(2):
