@@ -781,7 +781,8 @@ def run_ep(args):
         # gating, plan, counts read, dispatch push, wait, permute, gate/up, scan, combine
         # plan, push_chunks - 1 x (down GEMM, combine push), last down GEMM, then per token
         # chunk a push and a wait (and a reduce when the chunk holds tokens), send-side scan
-        C, ct = domain.combine_chunks, domain.chunk_tokens
+        C = domain.combine_chunks
+        ct = -(-T // C)  # every rank has T tokens: the call's chunks cover them
         reduces = min(C, -(-T // ct))
         launches = (1 + plan + 1 + 1 + 1 + permute + 1 + 1 + 1 + 2 * (layer.push_chunks - 1)
                     + 1 + 2 * C + reduces + 1)

@@ -155,10 +155,10 @@ class PeerDomain:
     ranks swap its CUDA IPC handle over the process group once, and the
     dispatch / combine kernels then store straight into the owner's buffer.
     `max_tokens` bounds the tokens of one rank per layer call.  The combine
-    runs in `combine_chunks` token chunks of ceil(max_tokens / combine_chunks)
-    tokens (the same on every rank): a rank reduces chunk c's tokens as soon
-    as every rank has pushed its rows for them, while later chunks are still
-    in flight.  close() (or leaving a `with` block) frees the buffers after a
+    runs in `combine_chunks` token chunks of ceil(T / combine_chunks) tokens,
+    T the largest token count of any rank in that call (the same chunks on
+    every rank): a rank reduces chunk c's tokens as soon as every rank has
+    pushed its rows for them, while later chunks are still in flight.  close() (or leaving a `with` block) frees the buffers after a
     barrier, so no peer still writes into them."""
 
     def __init__(self, max_tokens: int, hidden_dim: int, topk: int, group=None,
@@ -167,7 +167,6 @@ class PeerDomain:
         self.group, self.world_size, self.rank = group, ex.world_size, ex.rank
         self.max_tokens, self.hidden_dim, self.topk = max_tokens, hidden_dim, topk
         self.combine_chunks = max(1, min(int(combine_chunks), 16, max(max_tokens, 1)))
-        self.chunk_tokens = -(-max(max_tokens, 1) // self.combine_chunks)
         self._reduce_stream = None
         self._push_stream = None
         self.handle = _C.ep_domain_create(self.rank, self.world_size, max_tokens, hidden_dim, topk)
@@ -239,6 +238,7 @@ class PeerDispatch:
     recv_rows: torch.Tensor     # views of the domain's receive buffers
     recv_ids: torch.Tensor
     recv_w: torch.Tensor
+    chunk_tokens: int           # combine chunk size of this call, the same on every rank
 
     @property
     def valid_slots(self) -> int:
@@ -271,13 +271,19 @@ class HostMirror:
         return host.clone().view(src.shape)
 
 
-def _gather_counts(send_counts: torch.Tensor, domain: PeerDomain) -> torch.Tensor:
+def _gather_counts(send_counts: torch.Tensor, domain: PeerDomain, num_tokens: int):
+    """([G, G, 2] counts of every rank, the largest token count of any rank)
+    on the host, from one all-gather of each rank's [G, 2] counts and its
+    token count."""
     G = domain.world_size
     if G == 1:
-        return domain.mirror.read(send_counts.reshape(1, 1, 2))
-    every = torch.empty(G * G * 2, dtype=torch.int32, device=send_counts.device)
-    dist.all_gather_into_tensor(every, send_counts.reshape(-1), group=domain.group)
-    return domain.mirror.read(every.view(G, G, 2))
+        return domain.mirror.read(send_counts.reshape(1, 1, 2)), num_tokens
+    mine = torch.cat([send_counts.reshape(-1),
+                      torch.full((1,), num_tokens, dtype=torch.int32, device=send_counts.device)])
+    every = torch.empty(G * (2 * G + 1), dtype=torch.int32, device=send_counts.device)
+    dist.all_gather_into_tensor(every, mine, group=domain.group)
+    host = domain.mirror.read(every.view(G, 2 * G + 1))
+    return host[:, :2 * G].contiguous().view(G, G, 2), int(host[:, 2 * G].max())
 
 
 def peer_dispatch(domain: PeerDomain, hidden: torch.Tensor, topk_indices: torch.Tensor,
@@ -287,9 +293,12 @@ def peer_dispatch(domain: PeerDomain, hidden: torch.Tensor, topk_indices: torch.
     buffers and wait (bounded) for every rank's rows."""
     G, me = domain.world_size, domain.rank
     send_off, send_counts, pair_row, _ = steps.plan(topk_indices, num_experts, G)
-    counts = _gather_counts(send_counts, domain)
+    counts, t_max = _gather_counts(send_counts, domain, topk_indices.shape[0])
     if mark:
         mark("ep_plan")
+    # The combine's token chunks cover the largest rank's tokens (at most
+    # max_tokens), so every chunk holds tokens when the ranks are balanced.
+    chunk_tokens = -(-max(min(t_max, domain.max_tokens), 1) // domain.combine_chunks)
     epoch = domain.next_epoch()
     rows = int(counts[me, :, 0].sum())
     send_ids = _C.ep_dispatch_push(domain.handle, counts, hidden, topk_indices, topk_weights,
@@ -301,7 +310,8 @@ def peer_dispatch(domain: PeerDomain, hidden: torch.Tensor, topk_indices: torch.
         mark("ep_dispatch_wait")
     R = int(counts[:, me, 0].sum())
     return PeerDispatch(domain, epoch, counts, num_experts, topk_indices, pair_row, send_ids,
-                        domain.recv_rows[:R], domain.recv_ids[:R], domain.recv_w[:R])
+                        domain.recv_rows[:R], domain.recv_ids[:R], domain.recv_w[:R],
+                        chunk_tokens)
 
 
 def peer_combine_plan(pd: PeerDispatch, src_to_dest_map: torch.Tensor, steps=DeviceSteps):
@@ -334,7 +344,7 @@ def peer_combine_plan_chunked(pd: PeerDispatch, src_to_dest_map: torch.Tensor,
     dom = pd.domain
     slot_row = steps.slot_scan(pd.recv_ids)
     return _C.ep_combine_plan_chunks(dom.handle, src_to_dest_map, slot_row, pd.counts,
-                                     pd.recv_rows.shape[0], pd.valid_slots, dom.chunk_tokens,
+                                     pd.recv_rows.shape[0], pd.valid_slots, pd.chunk_tokens,
                                      dom.combine_chunks)
 
 
@@ -350,7 +360,7 @@ def peer_combine_chunked(pd: PeerDispatch, push_chunk: Callable[[int], None],
     pushes of the later chunks.  Returns the [T, H] bf16 output (bit-identical
     to the unchunked combine: the same per-token sums)."""
     dom = pd.domain
-    C, ct = dom.combine_chunks, dom.chunk_tokens
+    C, ct = dom.combine_chunks, pd.chunk_tokens
     T = pd.topk_indices.shape[0]
     G = dom.world_size
     main = torch.cuda.current_stream()

@@ -281,15 +281,15 @@ def test_combine_plan_chunks_lists_every_row_once():
         R, V = pd.recv_rows.shape[0], pd.valid_slots
         slot_row = P._C.ep_slot_scan(pd.recv_ids)
         plain = P._C.ep_combine_plan(dom.handle, s2d, slot_row, pd.counts, R, V)
+        ct = -(-1024 // C)
         dr, drow, dw, order, count = P._C.ep_combine_plan_chunks(
-            dom.handle, s2d, slot_row, pd.counts, R, V, dom.chunk_tokens, C)
+            dom.handle, s2d, slot_row, pd.counts, R, V, ct, C)
         EP.peer_combine(pd, permuted, s2d)  # completes the epoch
         sync_and_check_device_error()
         ids = pd.recv_ids.cpu().numpy()
     assert torch.equal(dr, plain[0]) and torch.equal(drow, plain[1])
     assert torch.equal(dw.view(torch.int32), plain[2].view(torch.int32))
-    ct = dom.chunk_tokens
-    assert ct == 342
+    assert pd.chunk_tokens == -(-T // C)  # the call's own chunks: T tokens on the one rank
     _, _, _, row_pair = P._C.ep_plan(dev(idx), E, 1)
     token = row_pair.cpu().numpy()[:R]
     p_of = s2d.cpu().numpy().reshape(R, k)
