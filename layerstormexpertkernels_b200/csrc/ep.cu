@@ -460,9 +460,49 @@ __global__ void ep_combine_plan_kernel(int32_t* __restrict__ dst_rank, int32_t* 
   }
 }
 
+// Row p of y becomes bf16(dst_w[p] * y[p]) at row dst_row[p] of rank
+// dst_rank[p]'s combine buffer (a row with an out-of-range plan is skipped).
+// One CTA per row; eight 16-byte loads in flight per thread before the
+// first store.
+__device__ __forceinline__ void push_combine_row(const PeerTable& peers, size_t back_off,
+                                                 const __nv_bfloat16* __restrict__ y,
+                                                 const int32_t* __restrict__ dst_rank,
+                                                 const int32_t* __restrict__ dst_row,
+                                                 const float* __restrict__ dst_w, int32_t p,
+                                                 int64_t cap_slots, int H, int world) {
+  const int nvec = H / 8;
+  const int32_t rk = __ldg(dst_rank + p);
+  const int32_t dr = __ldg(dst_row + p);
+  if (rk < 0 || rk >= world || dr < 0 || dr >= cap_slots) return;
+  const float wt = __ldg(dst_w + p);
+  const __nv_bfloat16* src = y + static_cast<int64_t>(p) * H;
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peers.base[rk] + back_off) +
+                       static_cast<int64_t>(dr) * H;
+  for (int v0 = threadIdx.x; v0 < nvec; v0 += 8 * kThreads) {
+    uint4 raw[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int v = v0 + u * kThreads;
+      if (v < nvec) raw[u] = ldg_nc_v4(src + v * 8);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int v = v0 + u * kThreads;
+      if (v >= nvec) break;
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[u]);
+      uint4 out;
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(&out);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o[q] = __float2bfloat16_rn(__fmul_rn(wt, __bfloat162float(e[q])));
+      *reinterpret_cast<uint4*>(dst + v * 8) = out;
+    }
+  }
+}
+
 // The combine without a GEMM in front (expert outputs already in memory):
-// row p of y becomes bf16(dst_w[p] * y[p]) at row dst_row[p] of rank
-// dst_rank[p]'s combine buffer; the last CTA publishes the combine epoch.
+// push_combine_row for the rows p0 .. p1-1, or with `order` for the rows of
+// chunk `chunk`'s list that lie in [p0, p1); then, if `publish`, the last CTA
+// publishes the epoch at flag_offset.
 __global__ void __launch_bounds__(kThreads) ep_combine_push_kernel(
     const __grid_constant__ PeerTable peers, size_t back_off, const __nv_bfloat16* __restrict__ y,
     const int32_t* __restrict__ dst_rank, const int32_t* __restrict__ dst_row,
@@ -470,46 +510,28 @@ __global__ void __launch_bounds__(kThreads) ep_combine_push_kernel(
     const int32_t* __restrict__ row_hi, int publish, int64_t cap_slots, int H, int world, int me,
     uint32_t* done, uint32_t epoch, const int32_t* __restrict__ order,
     const int32_t* __restrict__ order_count, int64_t order_stride, int chunk, size_t flag_offset) {
-  const int nvec = H / 8;
   const int32_t p0 = row_lo ? max(__ldg(row_lo), 0) : 0;
   const int32_t p1 = row_hi ? min(__ldg(row_hi), rows) : rows;
-  // With `order`: the rows order[d] of chunk `chunk`'s list that lie in
-  // [p0, p1); else the rows p0 .. p1-1.
-  if (order != nullptr) order += chunk * order_stride;
-  const int32_t d0 = order ? 0 : p0;
-  const int64_t listed = order ? static_cast<int64_t>(__ldg(order_count + chunk)) : 0;
-  const int32_t d1 = order ? static_cast<int32_t>(listed < order_stride ? listed : order_stride) : p1;
-  for (int32_t d = d0 + blockIdx.x; d < d1; d += gridDim.x) {
-    const int32_t p = order ? __ldg(order + d) : d;
-    if (p < p0 || p >= p1) continue;
-    const int32_t rk = __ldg(dst_rank + p);
-    const int32_t dr = __ldg(dst_row + p);
-    if (rk < 0 || rk >= world || dr < 0 || dr >= cap_slots) continue;
-    const float wt = __ldg(dst_w + p);
-    const __nv_bfloat16* src = y + static_cast<int64_t>(p) * H;
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peers.base[rk] + back_off) +
-                         static_cast<int64_t>(dr) * H;
-    // Eight 16-byte loads in flight per thread before the first store.
-    for (int v0 = threadIdx.x; v0 < nvec; v0 += 8 * kThreads) {
-      uint4 raw[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int v = v0 + u * kThreads;
-        if (v < nvec) raw[u] = ldg_nc_v4(src + v * 8);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int v = v0 + u * kThreads;
-        if (v >= nvec) break;
-        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[u]);
-        uint4 out;
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(&out);
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          o[q] = __float2bfloat16_rn(__fmul_rn(wt, __bfloat162float(e[q])));
-        *reinterpret_cast<uint4*>(dst + v * 8) = out;
-      }
+  if (order != nullptr) {
+    // A chunk list holds its rows in received-row order, grouped by source
+    // rank, so walking it in order would send every CTA's stores to one rank
+    // at a time (on every rank at once).  The walk interleaves `world` equal
+    // segments instead: v -> (v % world) * seg + v / world is a bijection of
+    // [0, world * seg), and the images past the list's end are skipped.
+    order += chunk * order_stride;
+    const int64_t listed = __ldg(order_count + chunk);
+    const int64_t n = listed < order_stride ? listed : order_stride;
+    const int64_t seg = (n + world - 1) / world;
+    for (int64_t v = blockIdx.x; v < seg * world; v += gridDim.x) {
+      const int64_t d = (v % world) * seg + v / world;
+      if (d >= n) continue;
+      const int32_t p = __ldg(order + d);
+      if (p < p0 || p >= p1) continue;
+      push_combine_row(peers, back_off, y, dst_rank, dst_row, dst_w, p, cap_slots, H, world);
     }
+  } else {
+    for (int32_t p = p0 + blockIdx.x; p < p1; p += gridDim.x)
+      push_combine_row(peers, back_off, y, dst_rank, dst_row, dst_w, p, cap_slots, H, world);
   }
   if (publish) grid_release_to_peers(peers, world, me, flag_offset, done, epoch);
   else __threadfence_system();  // ordered before the publishing call that follows on the stream
