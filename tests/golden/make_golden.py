@@ -159,21 +159,52 @@ def gemm_cases(ref, out_dir):
                         scores=scores.numpy(), out=out.numpy())
 
 
+def quant_cases(ref, out_dir):
+    """FP8 E4M3 block quantisation / dequantisation and NVFP4 dequantisation
+    (test_reference.py:19-107)."""
+    g = torch.Generator().manual_seed(61)
+    M, K = 6, 300  # 300 = two full 128-blocks and a ragged 44-wide one
+    x = torch.randn(M, K, generator=g)
+    x[1] *= 1000.0                 # large magnitudes
+    x[2, 128:256] = 0.0            # an all-zero block: scale 1.0
+    x[3] *= 1e-6                   # tiny magnitudes
+    x[4] = x[4].to(torch.bfloat16).float()  # bf16 inputs, as the layer's activations
+    x[5, :8] = torch.tensor([448.0, -448.0, 1.0, -1.0, 0.5, 3.0, -7.0, 0.0])
+    q, scales = ref.ref_dynamic_fp8_quant(x)
+    deq = ref.ref_fp8_dequant(q, scales, M, K)
+    np.savez_compressed(os.path.join(out_dir, "fp8_quant_m6_k300.npz"), x=x.numpy(),
+                        q=q.numpy(), scales=scales.numpy(), deq=deq.numpy())
+
+    M, N = 4, 64
+    packed = torch.randint(0, 256, (M, N // 2), generator=g, dtype=torch.int64).to(torch.uint8)
+    scales = torch.pow(2.0, torch.randint(-4, 5, (M, N // 16), generator=g).float())
+    out = ref.ref_nvfp4_dequant(packed, scales, M, N)
+    np.savez_compressed(os.path.join(out_dir, "nvfp4_dequant_m4_n64.npz"), packed=packed.numpy(),
+                        scales=scales.numpy(), out=out.numpy())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("LSEK_REFERENCE"),
                     help="checkout of the reference project (or set LSEK_REFERENCE)")
     ap.add_argument("--out", default=HERE)
+    ap.add_argument("--only", choices=["quant"], default=None,
+                    help="write only this group of fixtures")
     args = ap.parse_args()
     if not args.ref:
         ap.error("give --ref or set LSEK_REFERENCE to the reference checkout")
     ref = load_reference(args.ref)
+    if args.only == "quant":
+        quant_cases(ref, args.out)
+        print("wrote fixtures to", args.out)
+        return
     gating_cases(ref, args.out)
     adaptive_cases(ref, args.out)
     swiglu_cases(ref, args.out)
     permute_cases(args.out)
     combine_cases(args.out)
     gemm_cases(ref, args.out)
+    quant_cases(ref, args.out)
     print("wrote fixtures to", args.out)
 
 

@@ -156,3 +156,59 @@ def test_expert_forward_top1_matches_reference(golden_dir):
         y[s:t] = h @ d["w_down"][e].astype(np.float64).T
     out = y[s2d] * scores[:, None]
     assert np.allclose(out, d["out"], rtol=1e-4, atol=1e-4)
+
+
+# ---------------------------------------------------------------------------
+# block-scaled weight formats (the next row of the hot-path scope)
+# ---------------------------------------------------------------------------
+
+def test_fp8_block_quant_matches_reference(golden_dir):
+    from oracle import quant_oracle as Q
+    d = load(golden_dir, "fp8_quant_m6_k300")
+    q, scales = Q.dynamic_fp8_quant(d["x"])
+    assert np.array_equal(scales.view(np.uint32), d["scales"].view(np.uint32))
+    assert np.array_equal(q.view(np.uint32), d["q"].view(np.uint32))
+    assert scales[2, 1] == 1.0  # the all-zero block
+    deq = Q.fp8_dequant(d["q"], d["scales"])
+    assert np.array_equal(deq.view(np.uint32), d["deq"].view(np.uint32))
+
+
+def test_nvfp4_dequant_matches_reference(golden_dir):
+    from oracle import quant_oracle as Q
+    d = load(golden_dir, "nvfp4_dequant_m4_n64")
+    out = Q.nvfp4_dequant(d["packed"], d["scales"])
+    assert np.array_equal(out.view(np.uint32), d["out"].view(np.uint32))
+
+
+def test_e4m3_codes_round_trip_and_known_values():
+    from oracle import quant_oracle as Q
+    codes = np.arange(256, dtype=np.uint8)
+    vals = Q.e4m3_decode(codes)
+    nan = np.isnan(vals)
+    assert nan.sum() == 2 and nan[0x7F] and nan[0xFF]
+    known = {0x00: 0.0, 0x01: 2.0 ** -9, 0x07: 7 * 2.0 ** -9, 0x08: 2.0 ** -6, 0x38: 1.0,
+             0x3C: 1.5, 0x7E: 448.0, 0xB8: -1.0, 0xFE: -448.0}
+    for c, v in known.items():
+        assert vals[c] == np.float32(v), hex(c)
+    finite = codes[~nan]
+    assert np.array_equal(Q.e4m3_encode(vals[~nan]), finite)  # -0.0 keeps its sign code
+
+
+def test_e4m3_rounding_is_nearest_even():
+    from oracle import quant_oracle as Q
+    pos = Q.e4m3_decode(np.arange(0, 0x7F, dtype=np.uint8)).astype(np.float64)
+    mids = (pos[:-1] + pos[1:]) / 2.0
+    got = Q.e4m3_encode(mids.astype(np.float32))
+    lo_code = np.arange(0, 0x7E, dtype=np.uint8)
+    want = np.where(lo_code % 2 == 0, lo_code, lo_code + 1).astype(np.uint8)
+    assert np.array_equal(got, want)
+    rng = np.random.default_rng(7)
+    x = (rng.standard_normal(20000) * np.exp2(rng.integers(-12, 9, 20000))).astype(np.float32)
+    x = np.clip(x, -448, 448)
+    r = Q.e4m3_round(x).astype(np.float64)
+    allv = np.concatenate([-pos[::-1], pos])
+    best = np.abs(allv[None, :] - x.astype(np.float64)[:, None]).min(axis=1)
+    assert np.array_equal(np.abs(r - x), best)  # no representable value is nearer
+    assert Q.e4m3_encode(np.float32(1000.0)) == 0x7E
+    assert Q.e4m3_encode(np.float32(1000.0), saturate=False) == 0x7F
+    assert Q.e4m3_encode(np.float32(464.0), saturate=False) == 0x7E  # the tie goes to 448
