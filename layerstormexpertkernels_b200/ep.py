@@ -19,7 +19,8 @@ Rank g of G owns experts [g*E/G, (g+1)*E/G).  Per layer:
   5. combine: the packed slots go back (the reverse all-to-all, or a push
      into the source rank's combine buffer);
   6. the source rank sums each token's slots in slot order in fp32 from 0
-     and rounds once to bf16.
+     and rounds once to bf16 (over peer memory, per token chunk as soon as
+     every rank has pushed that chunk, beside the later chunks' pushes).
 
 Steps 4-6 reproduce moe_unpermute_bf16_perslot followed by
 moe_combine_reduce_slots_bf16_to_bf16 (smxx/permute/moe_permute.h:67-99 of
